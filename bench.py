@@ -1,0 +1,469 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-matmul hot path (cllm_inference's quant.cpp).
+
+Workload (the decode GEMV sweep over the Llama-3-8B layer
+shapes at M=1): one step = matmul_quant over every projection of all 32
+layers — q/o 4096x4096, k/v 1024x4096, gate/up 14336x4096 (Q4_K), down
+4096x14336 (Q6_K) — plus the 128256x4096 Q6_K lm_head: 225 calls, 4.84 GB of
+weights, each weight matrix distinct, so the 4.84 GB working set exceeds the
+126 MB L2 and every step streams from HBM.  Activations are fp32 N(0,1),
+quantized online to Q8_0 inside each call, as the reference does.  Weights are
+seeded synthetic GGML blocks (no model files).
+
+The printed JSON line:
+  value        weight+activation GB/s of the sweep, inputs resident in HBM
+  e2e          the same sweep through the host-buffer C ABI call
+               (cllm_cuda_matmul_quant with CLLM_HOST_IO): every call copies its
+               fp32 activations in from pinned memory and its outputs back
+  roofline     the dominant kernel (the Q4_K GEMV launches) against the
+               measured HBM copy bandwidth
+  cpu_baseline the reference's own quant.cpp (oracle/_ref) on the host cores
+  per_shape    GB/s per layer shape at M=1 and M=4, plus the Q8_0 and Q5_K
+               4096x4096 passes (each group timed after an L2 flush)
+  prefill      matmul_quant_batch 14336x4096 Q4_K at M in {64, 512, 2048}
+
+--impl reference runs the reference's CPU implementation on the same sweep.
+--gpus N (under torchrun) runs N independent replicas, one per GPU: weak
+scaling, no collective on the data path.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from cllm_inference_b200 import synth  # noqa: E402
+
+METRIC = "Q4_K GEMV HBM GB/s (% of peak); decode tok/s & prefill tok/s, 8B-shape Q4_K_M"
+UNIT = "GB/s"
+N_LAYERS = 32
+LAYER = [("q", synth.Q4_K, 4096, 4096), ("k", synth.Q4_K, 4096, 1024), ("v", synth.Q4_K, 4096, 1024),
+         ("o", synth.Q4_K, 4096, 4096), ("gate", synth.Q4_K, 4096, 14336), ("up", synth.Q4_K, 4096, 14336),
+         ("down", synth.Q6_K, 14336, 4096)]
+LM_HEAD = ("lm_head", synth.Q6_K, 4096, 128256)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def sweep_calls():
+    calls = [(l, *p) for l in range(N_LAYERS) for p in LAYER]
+    calls.append((0, *LM_HEAD))
+    return calls
+
+
+def call_bytes(t, k, n, m):
+    return synth.row_bytes(t, k) * n + 4 * m * k + 4 * m * n
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = f"/tmp/cllm_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline
+
+
+def reference_sweep_ms(ref, host_w, lm_w, x_host, y_host, n_threads, calls):
+    t0 = time.perf_counter()
+    for (l, name, t, k, n) in calls:
+        w = lm_w if name == "lm_head" else host_w[(l, name)]
+        ref.matmul_ptr(x_host[k].ctypes.data, w.ctypes.data, t, k, n, 1, y_host[n].ctypes.data, n_threads)
+    return (time.perf_counter() - t0) * 1e3
+
+
+def make_host_weights(n_distinct_layers, seed=0):
+    host_w = {}
+    for l in range(n_distinct_layers):
+        for (name, t, k, n) in LAYER:
+            host_w[(l, name)] = synth.make_weights(t, n, k, seed=seed + 100 * l + sum(map(ord, name)))
+    lm = synth.make_weights(LM_HEAD[1], LM_HEAD[3], LM_HEAD[2], seed=seed + 7)
+    return host_w, lm
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle.oracle import Reference, reference_available
+
+    if not reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libcllm_ref.so was not built"}))
+        return 0
+    ref = Reference()
+    n_threads = os.cpu_count() or 1
+    ref.pool(n_threads)
+    distinct = 8
+    host_w, lm = make_host_weights(distinct)
+    calls = [(l % distinct, name, t, k, n) for (l, name, t, k, n) in sweep_calls()]
+    x_host = {k: synth.make_activations(1, k, k)[0] for k in (4096, 14336)}
+    y_host = {n: np.empty(n, np.float32) for n in (4096, 1024, 14336, 128256)}
+    step_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
+    for _ in range(args.warmup):
+        reference_sweep_ms(ref, host_w, lm, x_host, y_host, n_threads, calls)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_sweep_ms(ref, host_w, lm, x_host, y_host, n_threads, calls)
+    ms = (time.perf_counter() - t0) * 1e3 / max(args.steps, 1)
+    value = step_bytes / (ms * 1e-3) / 1e9
+    sample = (f"full sweep per step: 225 matmul_quant calls (32 layers x q,k,v,o,gate,up,down + lm_head), "
+              f"M=1, weights cycling over {distinct} distinct synthetic layers ({step_bytes / 1e9:.2f} GB/step)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->int32, fp32 scales",
+            "data": "synthetic (seeded GGML blocks, N(0,1) activations)",
+            "config": {"workload": "decode GEMV sweep, Llama-3-8B shapes, M=1", "layers": N_LAYERS,
+                       "calls_per_step": len(calls)},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": n_threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def cpu_baseline(target_s=10.0):
+    """The reference's quant.cpp (oracle/_ref) on one 8B layer + lm_head, repeated for ~target_s."""
+    from oracle.oracle import Reference, reference_available
+
+    if not reference_available():
+        return None
+    ref = Reference()
+    n_threads = os.cpu_count() or 1
+    ref.pool(n_threads)
+    host_w, lm = make_host_weights(1, seed=3)
+    calls = [(0, name, t, k, n) for (name, t, k, n) in LAYER] + [(0, *LM_HEAD)]
+    x_host = {k: synth.make_activations(1, k, k)[0] for k in (4096, 14336)}
+    y_host = {n: np.empty(n, np.float32) for n in (4096, 1024, 14336, 128256)}
+    sample_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
+    reference_sweep_ms(ref, host_w, lm, x_host, y_host, n_threads, calls)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < target_s or reps < 2:
+        reference_sweep_ms(ref, host_w, lm, x_host, y_host, n_threads, calls)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(sample_bytes * reps / dt / 1e9, 3), "unit": UNIT, "cores": n_threads,
+            "kind": "reference",
+            "sample": (f"reference quant.cpp (g++ -O3, AVX2) matmul_quant on one 8B layer (q,k,v,o,gate,up,down) "
+                       f"+ lm_head, M=1, {reps} repetitions in {dt:.1f} s, ThreadPool({n_threads})")}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="skip the per-shape, prefill and e2e passes")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+
+    from cllm_inference_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    _lib.check(lib.cllm_cuda_init(dev.index))
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- resident inputs
+    weights = {}
+    for (l, name, t, k, n) in sweep_calls():
+        weights[(l, name)] = synth.make_weights_torch(t, n, k, seed=1000 * l + len(name) * 31 + n, device=dev)
+    xs = {k: torch.from_numpy(synth.make_activations(8, k, k)).to(dev) for k in (4096, 14336)}
+    ys = {n: torch.empty(8 * n, dtype=torch.float32, device=dev) for n in (4096, 1024, 14336, 128256)}
+    calls = sweep_calls()
+    step_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
+
+    def run_call(l, name, t, k, n, m=1):
+        w = weights[(l, name)]
+        return lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xs[k].data_ptr()), ctypes.c_void_p(w.data_ptr()), t,
+                                          None, k, n, m, ctypes.c_void_p(ys[n].data_ptr()), 0, sp)
+
+    def step(m=1):
+        for c in calls:
+            rc = run_call(*c, m=m)
+            if rc:
+                _lib.check(rc)
+
+    launches_per_step = 0
+    info = (ctypes.c_int * 8)()
+    for (l, name, t, k, n) in calls:
+        _lib.check(lib.cllm_cuda_matmul_plan(ctypes.c_void_p(weights[(l, name)].data_ptr()), t, k, n, 1, info, 8))
+        launches_per_step += info[0]
+    plan_q4k = list(info)  # overwritten below for the record
+    _lib.check(lib.cllm_cuda_matmul_plan(ctypes.c_void_p(weights[(0, "gate")].data_ptr()), synth.Q4_K, 4096,
+                                         14336, 1, info, 8))
+    plan_q4k = list(info)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.check(lib.cllm_cuda_check_device_status())
+
+    # ---- headline timed region
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    if dist is not None:
+        tt = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    ms_step = ms_total / args.steps
+    value = world * step_bytes * args.steps / (ms_total * 1e-3) / 1e9
+    _lib.check(lib.cllm_cuda_check_device_status())
+
+    # ---- roofline of the dominant kernel: the Q4_K GEMV launches, each bracketed by events
+    q4 = [c for c in calls if c[2] == synth.Q4_K]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(len(q4) * args.steps)]
+    i = 0
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        for c in calls:
+            if c[2] == synth.Q4_K:
+                evs[i][0].record(stream)
+                _lib.check(run_call(*c))
+                evs[i][1].record(stream)
+                i += 1
+            else:
+                _lib.check(run_call(*c))
+    torch.cuda.synchronize()
+    q4_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    q4_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in q4) / len(q4)
+    peak, peak_kind = measured_peaks()
+    achieved = q4_bytes / (q4_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "gemv_tma_kernel<Q4_K, M=1, fused quantize>",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "bytes_per_launch": int(q4_bytes), "avg_launch_us": round(q4_ms * 1e3, 2),
+                "traffic": None}
+    prof = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(prof):
+        try:
+            roofline["traffic"] = json.load(open(prof)).get("q4k_gemv_bytes_per_launch")
+        except Exception:
+            pass
+
+    extra = {}
+    if not args.quick:
+        extra = secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_call, calls, args)
+
+    line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32 (dp4a), fp32 scales",
+            "data": "synthetic (seeded GGML Q4_K/Q6_K blocks, N(0,1) fp32 activations)",
+            "config": {"workload": "decode GEMV sweep, Llama-3-8B shapes (BASELINE config 2), M=1",
+                       "layers": N_LAYERS, "calls_per_step": len(calls),
+                       "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (4.84 GB distinct weights/step)",
+                       "parallelism": f"{world} independent replicas (weak scaling)"},
+            "pct_of_peak": round(100.0 * value / world / peak, 2),
+            "gemv_tok_s": round(1e3 / ms_step, 2),
+            "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(), "plan_q4k_gate": plan_q4k}
+    line.update({k: v for k, v in extra.items() if k != "e2e"})
+    if "e2e" in extra:
+        line["e2e"] = extra["e2e"]
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
+def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_call, calls, args):
+    out = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn, reps=1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.random_(0, 255)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    # per shape: the 32 distinct copies of a layer matrix in a row, after an L2 flush
+    per = {}
+    shapes = [("q/o", "q"), ("k/v", "k"), ("gate/up", "gate"), ("down", "down")]
+    for m in (1, 4):
+        for label, name in shapes:
+            (_, t, k, n) = next(p for p in LAYER if p[0] == name)
+            for _ in range(2):
+                for l in range(N_LAYERS):
+                    _lib.check(run_call(l, name, t, k, n, m))
+            ms = min(timed(lambda: [_lib.check(run_call(l, name, t, k, n, m)) for l in range(N_LAYERS)])
+                     for _ in range(3))
+            per[f"{label} {synth.NAMES[t]} {n}x{k} M={m}"] = round(
+                N_LAYERS * call_bytes(t, k, n, m) / (ms * 1e-3) / 1e9, 1)
+        _lib.check(run_call(0, "lm_head", synth.Q6_K, 4096, 128256, m))
+        ms = min(timed(lambda: _lib.check(run_call(0, "lm_head", synth.Q6_K, 4096, 128256, m))) for _ in range(3))
+        per[f"lm_head Q6_K 128256x4096 M={m}"] = round(call_bytes(synth.Q6_K, 4096, 128256, m) / (ms * 1e-3) / 1e9, 1)
+    # extra pass: Q8_0 and Q5_K 4096x4096 (32 distinct copies each)
+    for t in (synth.Q8_0, synth.Q5_K):
+        ws = [synth.make_weights_torch(t, 4096, 4096, seed=77 + l, device=dev) for l in range(N_LAYERS)]
+        for m in (1, 4):
+            def go():
+                for w in ws:
+                    _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xs[4096].data_ptr()),
+                                                          ctypes.c_void_p(w.data_ptr()), t, None, 4096, 4096, m,
+                                                          ctypes.c_void_p(ys[4096].data_ptr()), 0, sp))
+            go()
+            ms = min(timed(go) for _ in range(3))
+            per[f"{synth.NAMES[t]} 4096x4096 M={m}"] = round(
+                N_LAYERS * call_bytes(t, 4096, 4096, m) / (ms * 1e-3) / 1e9, 1)
+        del ws
+    out["per_shape_gbs"] = per
+
+    # prefill: matmul_quant_batch 14336x4096 Q4_K
+    pre = {}
+    w = weights[(0, "gate")]
+    for M in (64, 512, 2048):
+        x = torch.from_numpy(synth.make_activations(M, 4096, M)).to(dev)
+        y = torch.empty(M * 14336, dtype=torch.float32, device=dev)
+
+        def go():
+            _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                                  synth.Q4_K, None, 4096, 14336, M, ctypes.c_void_p(y.data_ptr()),
+                                                  0, sp))
+        go()
+        ms = min(timed(go) for _ in range(2))
+        pre[f"M={M}"] = {"ms": round(ms, 3), "tok_s": round(M / (ms * 1e-3), 1),
+                         "tops": round(2.0 * M * 14336 * 4096 / (ms * 1e-3) / 1e12, 2)}
+    out["prefill_14336x4096_q4k"] = pre
+
+    # e2e: the same sweep through the host-buffer C ABI call
+    xh = {k: torch.from_numpy(synth.make_activations(1, k, k + 1)).pin_memory() for k in (4096, 14336)}
+    yh = {n: torch.empty(n, dtype=torch.float32).pin_memory() for n in (4096, 1024, 14336, 128256)}
+    h2d = sum(4 * k for (_, _, t, k, n) in calls)
+    d2h = sum(4 * n for (_, _, t, k, n) in calls)
+
+    def e2e_step():
+        for (l, name, t, k, n) in calls:
+            _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xh[k].data_ptr()),
+                                                  ctypes.c_void_p(weights[(l, name)].data_ptr()), t, None, k, n, 1,
+                                                  ctypes.c_void_p(yh[n].data_ptr()), _lib.HOST_IO, sp))
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    step_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
+    out["e2e"] = {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                  "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+                  "api": "cllm_cuda_matmul_quant(..., CLLM_HOST_IO) per projection, pinned host x/y"}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

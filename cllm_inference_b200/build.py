@@ -1,0 +1,81 @@
+"""Build the in-tree native libraries of cllm_inference_b200.
+
+* lib/libcllm_cuda.so   — the CUDA kernels and the C ABI (include/cllm_cuda.h),
+                           compiled for sm_100a only.
+* lib/libcllm_quant.so  — the C++20 drop-in for the reference's quant.hpp API
+                           (csrc/shim), linked against libcllm_cuda.so.
+* lib/quant_shim_test   — a C++ test driver for the shim (run by tests/).
+
+nvcc cross-compiles without a GPU, so this runs on the CPU build host too.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+LIB = os.path.join(PKG, "lib")
+INCLUDE = os.path.join(ROOT, "include")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
+CUDA_INC = os.path.join(CUDA_HOME, "include")
+CUDA_LIBDIR = os.path.join(CUDA_HOME, "lib64")
+
+CUDA_SO = os.path.join(LIB, "libcllm_cuda.so")
+SHIM_SO = os.path.join(LIB, "libcllm_quant.so")
+SHIM_TEST = os.path.join(LIB, "quant_shim_test")
+
+
+def _sources(*dirs):
+    out = []
+    for d in dirs:
+        for f in sorted(os.listdir(d)):
+            if f.endswith((".cu", ".cuh", ".h", ".hpp", ".cpp")):
+                out.append(os.path.join(d, f))
+    return out
+
+
+def _stale(target, deps):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _run(cmd, verbose):
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> None:
+    os.makedirs(LIB, exist_ok=True)
+    deps = _sources(CSRC) + [os.path.join(INCLUDE, "cllm_cuda.h")]
+    if force or ptxas_info or _stale(CUDA_SO, deps):
+        cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+               "-o", CUDA_SO, os.path.join(CSRC, "cllm_cuda.cu")]
+        if ptxas_info:
+            cmd[1:1] = ["-Xptxas", "-v"]
+        _run(cmd, verbose)
+    shim_dir = os.path.join(CSRC, "shim")
+    shim_deps = _sources(shim_dir, os.path.join(shim_dir, "cllm", "core")) + [CUDA_SO]
+    if os.path.exists(os.path.join(shim_dir, "quant_shim.cpp")):
+        if force or _stale(SHIM_SO, shim_deps):
+            _run(["g++", "-std=c++20", "-O2", "-Wall", "-Wextra", "-fPIC", "-shared",
+                  "-I", shim_dir, "-I", INCLUDE, "-I", CUDA_INC, "-o", SHIM_SO,
+                  os.path.join(shim_dir, "quant_shim.cpp"), "-L", LIB, "-lcllm_cuda",
+                  "-L", CUDA_LIBDIR, "-lcudart_static", "-ldl", "-lrt", "-pthread",
+                  "-Wl,-rpath,$ORIGIN"], verbose)
+        test_src = os.path.join(shim_dir, "quant_shim_test.cpp")
+        if os.path.exists(test_src) and (force or _stale(SHIM_TEST, shim_deps + [SHIM_SO])):
+            _run(["g++", "-std=c++20", "-O2", "-Wall", "-Wextra", "-I", shim_dir, "-I", INCLUDE,
+                  "-o", SHIM_TEST, test_src, "-L", LIB, "-lcllm_quant", "-lcllm_cuda",
+                  "-Wl,-rpath,$ORIGIN"], verbose)
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv)

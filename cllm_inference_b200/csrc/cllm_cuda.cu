@@ -1,0 +1,603 @@
+// C-ABI of the B200 quantized-matmul hot path (declarations: include/cllm_cuda.h).
+//
+// Host-side responsibilities:
+//   * argument checks and the reference's error strings (quant.cpp:423, 1379,
+//     1443, 1370), mapped to status codes — nothing throws across the ABI;
+//   * the weight registry: host ranges (GGUF mmap sections) uploaded once to
+//     HBM in native block layout, looked up by pointer for CLLM_W_HOST;
+//   * a per-device workspace for the quantized activations and host staging;
+//   * kernel selection (TMA-ring GEMV vs direct-load GEMV, rows-per-tile,
+//     pipeline depth) and launches.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/cllm_cuda.h"
+#include "common.cuh"
+#include "dequant.cuh"
+#include "gemv.cuh"
+#include "quantize.cuh"
+
+namespace cllm {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CLLM_CUDA_TRY(expr)                                                                    \
+    do {                                                                                       \
+        cudaError_t e_ = (expr);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(CLLM_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));        \
+    } while (0)
+
+int block_size_of(int t) {
+    switch (t) {
+        case 0: case 1: return 1;
+        case 2: case 3: case 6: case 7: case 8: case 9: return 32;
+        case 10: case 11: case 12: case 13: case 14: return 256;
+    }
+    return 1;
+}
+
+int64_t type_size_of(int t) {
+    switch (t) {
+        case 0: return 4;   case 1: return 2;   case 2: return 18;  case 3: return 20;
+        case 6: return 22;  case 7: return 24;  case 8: return 34;  case 9: return 36;
+        case 10: return 84; case 11: return 110; case 12: return 144; case 13: return 176;
+        case 14: return 210;
+    }
+    return 0;
+}
+
+bool has_vec_dot_of(int t) {
+    return t == kQ4_0 || t == kQ5_0 || t == kQ8_0 || t == kQ4_K || t == kQ5_K || t == kQ6_K;
+}
+
+struct DeviceInfo {
+    bool ready = false;
+    int sms = 0;
+    size_t max_smem_optin = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+struct Workspace {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+Workspace g_ws[64];
+
+struct WeightRange {
+    size_t bytes;
+    void* alloc;     // cudaMalloc'd block
+    uint8_t* dev;    // device address of host_base
+    int device;
+};
+std::map<uintptr_t, WeightRange> g_weights;  // keyed by host base address
+
+int current_device(int* dev) {
+    CLLM_CUDA_TRY(cudaGetDevice(dev));
+    if (*dev < 0 || *dev >= 64) return fail(CLLM_ERR_NO_DEVICE, "device index out of range");
+    return CLLM_OK;
+}
+
+int ensure_device(int* out_dev) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceInfo& di = g_dev[dev];
+    if (!di.ready) {
+        cudaDeviceProp prop;
+        CLLM_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major < 10)
+            return fail(CLLM_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                        dev, prop.major, prop.minor);
+        di.sms = prop.multiProcessorCount;
+        di.max_smem_optin = prop.sharedMemPerBlockOptin;
+        di.ready = true;
+    }
+    *out_dev = dev;
+    return CLLM_OK;
+}
+
+// Grow the device workspace to at least `bytes` (never shrinks).
+int workspace(int dev, size_t bytes, uint8_t** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Workspace& ws = g_ws[dev];
+    if (ws.cap < bytes) {
+        if (ws.ptr) {
+            CLLM_CUDA_TRY(cudaDeviceSynchronize());  // a previous call may still use it
+            CLLM_CUDA_TRY(cudaFree(ws.ptr));
+            ws.ptr = nullptr;
+            ws.cap = 0;
+        }
+        const size_t cap = std::max<size_t>(bytes + (bytes >> 2), size_t(4) << 20);
+        CLLM_CUDA_TRY(cudaMalloc(&ws.ptr, cap));
+        ws.cap = cap;
+    }
+    *out = static_cast<uint8_t*>(ws.ptr);
+    return CLLM_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int lookup(const void* host_ptr, const uint8_t** dev_ptr, size_t* avail) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const uintptr_t h = reinterpret_cast<uintptr_t>(host_ptr);
+    auto it = g_weights.upper_bound(h);
+    if (it == g_weights.begin()) return CLLM_ERR_NOT_REGISTERED;
+    --it;
+    if (h >= it->first + it->second.bytes) return CLLM_ERR_NOT_REGISTERED;
+    *dev_ptr = it->second.dev + (h - it->first);
+    if (avail) *avail = it->first + it->second.bytes - h;
+    return CLLM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kernel tables
+typedef void (*GemvFn)(GemvParams);
+
+template <int T>
+GemvFn gemv_fn(bool tma, bool fused, bool emit, int m) {
+    if (emit) return tma ? gemv_tma_kernel<T, 1, true, false> : gemv_direct_kernel<T, 1, true>;
+#define CLLM_CASE(MM)                                                                     \
+    case MM:                                                                              \
+        return !tma ? gemv_direct_kernel<T, MM, false>                                    \
+                    : (fused ? gemv_tma_kernel<T, MM, false, true> : gemv_tma_kernel<T, MM, false, false>);
+    switch (m) {
+        CLLM_CASE(1) CLLM_CASE(2) CLLM_CASE(3) CLLM_CASE(4)
+        CLLM_CASE(5) CLLM_CASE(6) CLLM_CASE(7) CLLM_CASE(8)
+    }
+#undef CLLM_CASE
+    return nullptr;
+}
+
+GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
+    switch (type) {
+        case kQ4_0: return gemv_fn<kQ4_0>(tma, fused, emit, m);
+        case kQ5_0: return gemv_fn<kQ5_0>(tma, fused, emit, m);
+        case kQ8_0: return gemv_fn<kQ8_0>(tma, fused, emit, m);
+        case kQ4_K: return gemv_fn<kQ4_K>(tma, fused, emit, m);
+        case kQ5_K: return gemv_fn<kQ5_K>(tma, fused, emit, m);
+        case kQ6_K: return gemv_fn<kQ6_K>(tma, fused, emit, m);
+    }
+    return nullptr;
+}
+
+constexpr uint32_t kSmemPerCta = 110 * 1024;  // two CTAs per SM
+constexpr uint32_t kTileTarget = 32 * 1024;   // bytes of weights per tile
+constexpr uint32_t kFusedActMax = 40 * 1024;  // largest quantized activation kept in shared memory
+
+struct GemvPlan {
+    bool tma, fused;
+    int rows_per_tile, wpr, num_tiles, stages, grid;
+    uint32_t stage_bytes;
+    size_t smem;
+};
+
+// Tile / pipeline choice.  want_fused: quantize the activations inside the
+// kernel when they fit (m rows of K).
+GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, int m, bool want_fused,
+                   const DeviceInfo& di) {
+    GemvPlan pl{};
+    const int upr = units_per_row(type, K);
+    const int max_wpr = std::max(1, std::min(kGemvWarps, upr / 32));
+    int R = kGemvWarps;
+    while (R > 1 && (int64_t)R * row_bytes > kTileTarget) R >>= 1;
+    while (R > 1 && (N + R - 1) / R < 2 * di.sms && kGemvWarps / (R >> 1) <= max_wpr) R >>= 1;
+    while (kGemvWarps / R > max_wpr) R <<= 1;  // keep every warp of a row busy
+    pl.rows_per_tile = R;
+    pl.wpr = kGemvWarps / R;
+    pl.num_tiles = (N + R - 1) / R;
+    pl.stage_bytes = (uint32_t)(((int64_t)R * row_bytes + 127) & ~int64_t(127));
+    const uint32_t act = (fused_act_bytes(m, K) + 127u) / 128u * 128u;
+    pl.fused = want_fused && K > 0 && act <= kFusedActMax;
+    const size_t fixed = kGemvSmemHeader + (pl.fused ? act : 0);
+    const size_t limit = di.max_smem_optin > 1024 ? di.max_smem_optin - 1024 : 0;
+    pl.tma = K > 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (row_bytes & 15) == 0 &&
+             fixed + 2ull * pl.stage_bytes <= limit;
+    if (!pl.tma) pl.fused = false;
+    if (pl.tma) {
+        const size_t budget = std::max<size_t>(kSmemPerCta, fixed + 2ull * pl.stage_bytes);
+        int S = (int)std::min<size_t>(8, (budget - fixed) / pl.stage_bytes);
+        if (S < 2) S = 2;
+        pl.stages = S;
+        pl.smem = fixed + (size_t)S * pl.stage_bytes;
+        const int per_sm = pl.smem <= kSmemPerCta ? 2 : 1;
+        pl.grid = std::min(pl.num_tiles, per_sm * di.sms);
+    } else {
+        pl.stages = 0;
+        pl.smem = 0;
+        pl.grid = std::min(pl.num_tiles, 4 * di.sms);
+    }
+    if (pl.grid < 1) pl.grid = 1;
+    return pl;
+}
+
+int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams& p, cudaStream_t st) {
+    GemvFn fn = select_gemv(type, pl.tma, pl.fused, emit, m);
+    if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no kernel for type %d, %d rows", type, m);
+    if (pl.tma) {
+        CLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)pl.smem));
+    }
+    fn<<<pl.grid, kGemvThreads, pl.smem, st>>>(p);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+void fill_plan(GemvParams& p, const GemvPlan& pl) {
+    p.rows_per_tile = pl.rows_per_tile;
+    p.wpr = pl.wpr;
+    p.num_tiles = pl.num_tiles;
+    p.stages = pl.stages;
+    p.stage_bytes = pl.stage_bytes;
+}
+
+int launch_quantize(const float* x, int64_t n, int rows, float* sc, int8_t* qs, int32_t* bs,
+                    uint8_t* fl, const DeviceInfo& di, cudaStream_t st) {
+    const int64_t total = (n / 32) * rows;
+    if (total == 0) return CLLM_OK;
+    const int64_t warps_per_cta = kGemvThreads / 32;
+    const int64_t grid = std::min<int64_t>((total + warps_per_cta - 1) / warps_per_cta, 16LL * di.sms);
+    quantize_q8_0_kernel<<<(unsigned)grid, kGemvThreads, 0, st>>>(x, n, total, sc, qs, bs, fl);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+// Layout of the quantized activations inside the workspace.
+struct ActLayout {
+    size_t qs, dx, bs, fl, end;
+};
+ActLayout act_layout(int m, int K, size_t at) {
+    ActLayout L;
+    const size_t nb = (size_t)K / 32;
+    L.qs = at;
+    L.dx = align256(L.qs + (size_t)m * K);
+    L.bs = align256(L.dx + (size_t)m * nb * 4);
+    L.fl = align256(L.bs + (size_t)m * nb * 4);
+    L.end = align256(L.fl + (size_t)m * nb);
+    return L;
+}
+
+}  // namespace
+}  // namespace cllm
+
+using namespace cllm;
+
+extern "C" {
+
+int cllm_cuda_last_error(char* buf, size_t n) {
+    if (buf && n) {
+        const size_t k = std::min(n - 1, g_last_error.size());
+        std::memcpy(buf, g_last_error.data(), k);
+        buf[k] = 0;
+    }
+    return (int)g_last_error.size();
+}
+
+int cllm_cuda_block_size(int type) { return block_size_of(type); }
+int64_t cllm_cuda_type_size(int type) { return type_size_of(type); }
+int cllm_cuda_has_vec_dot(int type) { return has_vec_dot_of(type) ? 1 : 0; }
+
+int cllm_cuda_init(int device) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0)
+        return fail(CLLM_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+    if (device < 0 || device >= count) return fail(CLLM_ERR_INVALID_ARG, "device %d of %d", device, count);
+    CLLM_CUDA_TRY(cudaSetDevice(device));
+    int dev;
+    return ensure_device(&dev);
+}
+
+int cllm_cuda_register_weights(const void* host_base, size_t bytes, void** dev_base) {
+    if (!host_base || bytes == 0) return fail(CLLM_ERR_INVALID_ARG, "register_weights: empty range");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const uintptr_t h = reinterpret_cast<uintptr_t>(host_base);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_weights.upper_bound(h + bytes - 1);
+        if (it != g_weights.begin()) {
+            --it;
+            if (it->first + it->second.bytes > h)
+                return fail(CLLM_ERR_INVALID_ARG, "register_weights: range overlaps a registered range");
+        }
+    }
+    const size_t lead = h & 255;  // keep the host address's offset modulo 256
+    void* alloc = nullptr;
+    CLLM_CUDA_TRY(cudaMalloc(&alloc, bytes + lead));
+    uint8_t* dev_ptr = static_cast<uint8_t*>(alloc) + lead;
+    cudaError_t e = cudaMemcpy(dev_ptr, host_base, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(alloc);
+        return fail(CLLM_ERR_CUDA, "register_weights: upload failed: %s", cudaGetErrorString(e));
+    }
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        g_weights[h] = WeightRange{bytes, alloc, dev_ptr, dev};
+    }
+    if (dev_base) *dev_base = dev_ptr;
+    return CLLM_OK;
+}
+
+int cllm_cuda_unregister_weights(const void* host_base) {
+    void* alloc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_weights.find(reinterpret_cast<uintptr_t>(host_base));
+        if (it == g_weights.end()) return fail(CLLM_ERR_NOT_REGISTERED, "unregister_weights: unknown range");
+        alloc = it->second.alloc;
+        g_weights.erase(it);
+    }
+    CLLM_CUDA_TRY(cudaFree(alloc));
+    return CLLM_OK;
+}
+
+int cllm_cuda_lookup_weights(const void* host_ptr, const void** dev_ptr) {
+    if (!dev_ptr) return fail(CLLM_ERR_INVALID_ARG, "lookup_weights: null output");
+    const uint8_t* d = nullptr;
+    if (lookup(host_ptr, &d, nullptr) != CLLM_OK)
+        return fail(CLLM_ERR_NOT_REGISTERED, "weight pointer %p is not inside a registered range", host_ptr);
+    *dev_ptr = d;
+    return CLLM_OK;
+}
+
+int cllm_cuda_quantize_q8_0(const float* x, int64_t n, int rows, float* scales, int8_t* qs,
+                            int32_t* bsums, void* stream) {
+    if (n < 0 || rows < 0) return fail(CLLM_ERR_INVALID_ARG, "quantize_row_q8_0: negative size");
+    if (n % 32 != 0) return fail(CLLM_ERR_BLOCK_MULTIPLE, "quantize_row_q8_0: n not divisible by 32");
+    if (n == 0 || rows == 0) return CLLM_OK;
+    if (!x || !scales || !qs || !bsums) return fail(CLLM_ERR_INVALID_ARG, "quantize_row_q8_0: null pointer");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    return launch_quantize(x, n, rows, scales, qs, bsums, nullptr, g_dev[dev],
+                           static_cast<cudaStream_t>(stream));
+}
+
+int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float* bias, int in_dim,
+                           int out_dim, int n_rows, float* y, unsigned flags, void* stream) {
+    const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
+    if (n_rows <= 0) return CLLM_OK;  // quant.cpp:1436
+    if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))
+        return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
+    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
+    const int bsz = block_size_of(type);
+    if (in_dim % bsz != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
+    if (!has_vec_dot_of(type))
+        return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (out_dim == 0) return CLLM_OK;
+    if (!y || (in_dim > 0 && (!x || !w))) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    const int64_t row_bytes = (int64_t)(in_dim / bsz) * type_size_of(type);
+    const uint8_t* wd = static_cast<const uint8_t*>(w);
+    if (flags & CLLM_W_HOST) {
+        size_t avail = 0;
+        if (lookup(w, &wd, &avail) != CLLM_OK)
+            return fail(CLLM_ERR_NOT_REGISTERED, "%s: weight pointer %p is not inside a registered range",
+                        fname, w);
+        if ((uint64_t)row_bytes * (uint64_t)out_dim > avail)
+            return fail(CLLM_ERR_INVALID_ARG, "%s: weight matrix runs past its registered range", fname);
+    }
+
+    const int mchunk = std::min(n_rows, 8);
+    const ActLayout L = act_layout(mchunk, in_dim, 0);
+    size_t off_x = L.end, off_b = L.end, off_y = L.end, total = L.end;
+    if (flags & CLLM_X_HOST) {
+        off_x = total;
+        total = align256(total + (size_t)n_rows * in_dim * 4);
+        off_b = total;
+        if (bias) total = align256(total + (size_t)out_dim * 4);
+    }
+    if (flags & CLLM_Y_HOST) {
+        off_y = total;
+        total = align256(total + (size_t)n_rows * out_dim * 4);
+    }
+    uint8_t* ws;
+    if (int rc = workspace(dev, total, &ws)) return rc;
+
+    const float* xd = x;
+    const float* bd = bias;
+    float* yd = y;
+    if (flags & CLLM_X_HOST) {
+        xd = reinterpret_cast<float*>(ws + off_x);
+        CLLM_CUDA_TRY(cudaMemcpyAsync((void*)xd, x, (size_t)n_rows * in_dim * 4, cudaMemcpyHostToDevice, st));
+        if (bias) {
+            bd = reinterpret_cast<float*>(ws + off_b);
+            CLLM_CUDA_TRY(cudaMemcpyAsync((void*)bd, bias, (size_t)out_dim * 4, cudaMemcpyHostToDevice, st));
+        }
+    }
+    if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
+
+    for (int t0 = 0; t0 < n_rows; t0 += 8) {
+        const int m = std::min(8, n_rows - t0);
+        const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di);
+        GemvParams p{};
+        p.w = wd;
+        p.row_bytes = row_bytes;
+        p.K = in_dim;
+        p.N = out_dim;
+        p.x = xd + (size_t)t0 * in_dim;
+        p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
+        p.dx = reinterpret_cast<float*>(ws + L.dx);
+        p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
+        p.fl = ws + L.fl;
+        p.bias = bd;
+        p.y = yd + (size_t)t0 * out_dim;
+        p.partials = nullptr;
+        fill_plan(p, pl);
+        if (!pl.fused) {
+            if (int rc = launch_quantize(p.x, in_dim, m, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
+                                         const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
+                return rc;
+        }
+        if (int rc = launch_gemv(type, false, m, pl, p, st)) return rc;
+    }
+    if (flags & CLLM_Y_HOST) {
+        CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
+        CLLM_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return CLLM_OK;
+}
+
+int cllm_cuda_matmul_q8(const float* scales, const int8_t* qs, const int32_t* bsums, const void* w,
+                        int type, const float* bias, int in_dim, int out_dim, int n_rows, float* y,
+                        void* stream) {
+    const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
+    if (n_rows <= 0) return CLLM_OK;
+    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
+    if (in_dim % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (out_dim == 0) return CLLM_OK;
+    if (!w || !y || (in_dim > 0 && (!scales || !qs || !bsums)))
+        return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
+    const int64_t nb = in_dim / 32;
+    uint8_t* ws;
+    if (int rc = workspace(dev, align256((size_t)n_rows * nb) + 256, &ws)) return rc;
+    const int64_t total = nb * n_rows;
+    if (total > 0) {
+        const int64_t grid = std::min<int64_t>((total + 7) / 8, 16LL * di.sms);
+        q8_flags_kernel<<<(unsigned)grid, 256, 0, st>>>(qs, total, ws);
+        CLLM_CUDA_TRY(cudaGetLastError());
+    }
+    for (int t0 = 0; t0 < n_rows; t0 += 8) {
+        const int m = std::min(8, n_rows - t0);
+        const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, m,
+                                      false, di);
+        GemvParams p{};
+        p.w = static_cast<const uint8_t*>(w);
+        p.row_bytes = row_bytes;
+        p.K = in_dim;
+        p.N = out_dim;
+        p.qx = qs + (size_t)t0 * in_dim;
+        p.dx = scales + (size_t)t0 * nb;
+        p.bs = bsums + (size_t)t0 * nb;
+        p.fl = ws + (size_t)t0 * nb;
+        p.bias = bias;
+        p.y = y + (size_t)t0 * out_dim;
+        fill_plan(p, pl);
+        if (int rc = launch_gemv(type, false, m, pl, p, st)) return rc;
+    }
+    return CLLM_OK;
+}
+
+int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim, int out_dim,
+                           int n_rows, int32_t* partials, void* stream) {
+    if (in_dim < 0 || out_dim < 0 || n_rows < 0) return fail(CLLM_ERR_INVALID_ARG, "row_partials: negative size");
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (in_dim % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "matmul_quant: in_dim not divisible by block size");
+    if (n_rows == 0 || out_dim == 0 || in_dim == 0) return CLLM_OK;
+    if (!qs || !w || !partials) return fail(CLLM_ERR_INVALID_ARG, "row_partials: null pointer");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
+    const int ppr = (type == kQ6_K ? 2 : 1) * (in_dim / 32);
+    const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, 1,
+                                  false, di);
+    // The dot kernels also read the block scales/sums (zeros here: they do not
+    // affect the integer partials) and the per-block "-128 present" flags.
+    // All flags are set, so the sign-trick correction is evaluated on every
+    // block; it is zero wherever no -128 activation meets a negative weight.
+    const ActLayout L = act_layout(1, in_dim, 0);
+    uint8_t* ws;
+    if (int rc = workspace(dev, L.end, &ws)) return rc;
+    CLLM_CUDA_TRY(cudaMemsetAsync(ws + L.dx, 0, L.fl - L.dx, st));
+    CLLM_CUDA_TRY(cudaMemsetAsync(ws + L.fl, 1, L.end - L.fl, st));
+    for (int t = 0; t < n_rows; ++t) {
+        GemvParams p{};
+        p.w = static_cast<const uint8_t*>(w);
+        p.row_bytes = row_bytes;
+        p.K = in_dim;
+        p.N = out_dim;
+        p.qx = qs + (size_t)t * in_dim;
+        p.dx = reinterpret_cast<float*>(ws + L.dx);
+        p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
+        p.fl = ws + L.fl;
+        p.y = nullptr;
+        p.partials = partials + (size_t)t * out_dim * ppr;
+        fill_plan(p, pl);
+        if (int rc = launch_gemv(type, true, 1, pl, p, st)) return rc;
+    }
+    return CLLM_OK;
+}
+
+int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream) {
+    if (n < 0) return fail(CLLM_ERR_INVALID_ARG, "dequantize: negative size");
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
+    if (n % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "dequantize: n not divisible by block size");
+    if (n == 0) return CLLM_OK;
+    if (!src || !dst) return fail(CLLM_ERR_INVALID_ARG, "dequantize: null pointer");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const int64_t grid = std::min<int64_t>((n + 255) / 256, 32LL * g_dev[dev].sms);
+    dequantize_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t*>(src), type, n, dst);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int n_rows, int* info,
+                          int n_info) {
+    if (!info || n_info < 0 || in_dim < 0 || out_dim < 0)
+        return fail(CLLM_ERR_INVALID_ARG, "matmul_plan: bad arguments");
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (in_dim % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "matmul_quant: in_dim not divisible by block size");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
+    const int m = std::max(1, std::min(8, n_rows));
+    const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, m, true,
+                                  g_dev[dev]);
+    const int chunks = n_rows <= 0 ? 0 : (n_rows + 7) / 8;
+    const int vals[8] = {chunks * (pl.fused ? 1 : 2), pl.tma, pl.fused, pl.rows_per_tile, pl.wpr,
+                         pl.stages, pl.grid, (int)pl.smem};
+    for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];
+    return CLLM_OK;
+}
+
+int cllm_cuda_check_device_status(void) {
+    CLLM_CUDA_TRY(cudaDeviceSynchronize());
+    int status = 0, zero = 0;
+    CLLM_CUDA_TRY(cudaMemcpyFromSymbol(&status, g_device_status, sizeof(int)));
+    CLLM_CUDA_TRY(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+    if (status == kStatusTimeout)
+        return fail(CLLM_ERR_KERNEL_TIMEOUT, "a kernel's bounded wait expired (pipeline copy never landed)");
+    return CLLM_OK;
+}
+
+}  // extern "C"

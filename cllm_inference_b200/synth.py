@@ -1,0 +1,89 @@
+"""Seeded synthetic GGML weight blocks and activations.
+
+There are no model files in this build; every weight matrix is generated from
+a seed with the value distributions below.  The byte layouts are GGML's
+(cllm_inference include/cllm/core/quant.hpp:13-27, src/core/quant.cpp:340-369):
+
+=====  =====  ==========================================================
+type   bytes  fields and synthetic distribution
+=====  =====  ==========================================================
+Q4_K   144    d f16 ~U(1e-3,2e-2), dmin f16 ~U(0,1e-2), 12 packed 6-bit
+              scale/min bytes ~U{0..255} (each unpacks to U{0..63}),
+              128 B of nibbles ~U{0..15}
+Q5_K   176    as Q4_K plus 32 B of high bits ~U
+Q6_K   210    128 B low nibbles, 64 B high pairs ~U; 16 int8 scales
+              ~U{-32..31}; d f16 ~U(1e-3,2e-2) at offset 208
+Q8_0   34     d f16 ~U(1e-3,2e-2), 32 int8 ~U
+Q4_0   18     d f16 ~U(1e-3,2e-2), 16 B nibbles ~U
+Q5_0   22     d f16 ~U(1e-3,2e-2), 4 B high bits, 16 B nibbles ~U
+=====  =====  ==========================================================
+
+Activations are fp32 ~N(0, 1).  ``make_weights`` (numpy) feeds the CPU checks;
+``make_weights_torch`` builds the same distributions directly in device memory
+for the benchmark, where only throughput is measured.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 6, 8, 12, 13, 14
+BLOCK = {Q4_0: 32, Q5_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+TSIZE = {Q4_0: 18, Q5_0: 22, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+BY_NAME = {v: k for k, v in NAMES.items()}
+
+
+def row_bytes(t: int, k: int) -> int:
+    return (k // BLOCK[t]) * TSIZE[t]
+
+
+def _f16_bytes(vals: np.ndarray) -> np.ndarray:
+    return vals.astype(np.float16).view(np.uint8).reshape(-1, 2)
+
+
+def make_weights(t: int, n_rows: int, k: int, seed: int) -> np.ndarray:
+    """[n_rows * row_bytes] uint8 of seeded synthetic blocks of type t."""
+    if k % BLOCK[t]:
+        raise ValueError("k must be a multiple of the block size")
+    rng = np.random.default_rng(seed)
+    nblk = n_rows * (k // BLOCK[t])
+    ts = TSIZE[t]
+    w = rng.integers(0, 256, size=(nblk, ts), dtype=np.uint8)
+    if nblk == 0:
+        return w.reshape(-1)
+    d = rng.uniform(1e-3, 2e-2, size=nblk)
+    if t == Q6_K:
+        w[:, 192:208] = rng.integers(-32, 32, size=(nblk, 16), dtype=np.int8).view(np.uint8)
+        w[:, 208:210] = _f16_bytes(d)
+    else:
+        w[:, 0:2] = _f16_bytes(d)
+        if t in (Q4_K, Q5_K):
+            w[:, 2:4] = _f16_bytes(rng.uniform(0.0, 1e-2, size=nblk))
+    return w.reshape(-1)
+
+
+def make_activations(m: int, k: int, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed).standard_normal((m, k), dtype=np.float32)
+
+
+def make_weights_torch(t: int, n_rows: int, k: int, seed: int, device="cuda"):
+    """Same distributions as make_weights, generated in device memory (torch uint8 [bytes])."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    nblk = n_rows * (k // BLOCK[t])
+    ts = TSIZE[t]
+    w = torch.randint(0, 256, (nblk, ts), dtype=torch.uint8, device=device, generator=g)
+    d = (torch.rand(nblk, device=device, generator=g) * (2e-2 - 1e-3) + 1e-3).half()
+    d = d.view(torch.uint8).view(nblk, 2)
+    if t == Q6_K:
+        w[:, 192:208] = torch.randint(-32, 32, (nblk, 16), dtype=torch.int8, device=device,
+                                      generator=g).view(torch.uint8)
+        w[:, 208:210] = d
+    else:
+        w[:, 0:2] = d
+        if t in (Q4_K, Q5_K):
+            dm = (torch.rand(nblk, device=device, generator=g) * 1e-2).half()
+            w[:, 2:4] = dm.view(torch.uint8).view(nblk, 2)
+    return w.view(-1)

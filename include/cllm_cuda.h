@@ -1,0 +1,147 @@
+/*
+ * cllm_cuda.h — C ABI of the B200 (sm_100a) quantized-matmul hot path.
+ *
+ * Drop-in replacement for the quant API of cllm_inference
+ * (include/cllm/core/quant.hpp:90-151, src/core/quant.cpp:340-1475 in the
+ * reference project).  Plain C: pointers, sizes and ints only.  Every entry
+ * point returns CLLM_OK (0) or a negative CLLM_ERR_* code and never throws;
+ * cllm_cuda_last_error() returns the message of the calling thread's last
+ * failure, using the reference's own exception strings where it has one.
+ *
+ * Weight types use the GGML numbering of GgmlType (quant.hpp:13-27).  The six
+ * with an integer dot kernel (quant.hpp:129-130) are accepted by the matmul
+ * entry points; every other type is rejected with CLLM_ERR_UNSUPPORTED_TYPE —
+ * there is no CPU fallback.
+ *
+ * Streams are passed as `void*` (a cudaStream_t; NULL = the legacy default
+ * stream).  Calls on one stream are not re-entrant: use one stream per engine.
+ */
+#ifndef CLLM_CUDA_H
+#define CLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define CLLM_OK 0
+#define CLLM_ERR_INVALID_ARG -1      /* null pointer, negative size, bad flag */
+#define CLLM_ERR_UNSUPPORTED_TYPE -2 /* type without an integer dot kernel */
+#define CLLM_ERR_BLOCK_MULTIPLE -3   /* in_dim not a multiple of the block size */
+#define CLLM_ERR_CUDA -4             /* a CUDA runtime call failed */
+#define CLLM_ERR_NOT_REGISTERED -5   /* host weight pointer outside every registered range */
+#define CLLM_ERR_NO_DEVICE -6        /* no usable sm_100 device */
+#define CLLM_ERR_KERNEL_TIMEOUT -7   /* a kernel's bounded wait expired (status flag set on device) */
+#define CLLM_ERR_TOO_LARGE -8        /* a size beyond what an entry point supports */
+
+/* ---- GGML type ids (quant.hpp:13-27) ----------------------------------- */
+#define CLLM_TYPE_Q4_0 2
+#define CLLM_TYPE_Q5_0 6
+#define CLLM_TYPE_Q8_0 8
+#define CLLM_TYPE_Q4_K 12
+#define CLLM_TYPE_Q5_K 13
+#define CLLM_TYPE_Q6_K 14
+
+/* ---- cllm_cuda_matmul_quant flags -------------------------------------- */
+#define CLLM_X_HOST 1u /* x and bias are host pointers (copied in on the stream) */
+#define CLLM_Y_HOST 2u /* y is a host pointer; the call synchronizes the stream */
+#define CLLM_W_HOST 4u /* w is a host pointer inside a range given to cllm_cuda_register_weights */
+#define CLLM_HOST_IO (CLLM_X_HOST | CLLM_Y_HOST)
+
+/* Select and initialise the device (cudaSetDevice + capability check).
+ * Replaces nothing in the reference (the CPU engine has no device); the
+ * quant.hpp shim calls it once on first use. */
+int cllm_cuda_init(int device);
+
+/* quant.cpp:340-352 — elements per block; 1 for F32/F16 and unknown types. */
+int cllm_cuda_block_size(int type);
+
+/* quant.cpp:354-369 — bytes per block; 0 for unknown types. */
+int64_t cllm_cuda_type_size(int type);
+
+/* quant.cpp:1347-1357 — 1 for Q4_0/Q5_0/Q8_0/Q4_K/Q5_K/Q6_K, else 0. */
+int cllm_cuda_has_vec_dot(int type);
+
+/* Upload [host_base, host_base+bytes) — e.g. a GGUF mmap'd data section
+ * (gguf.cpp:171-189) — to HBM once, in its native block layout, and remember
+ * the mapping so later calls can pass weight pointers into that host range
+ * with CLLM_W_HOST.  The device copy keeps the host address's offset modulo
+ * 256, so rows aligned on the host are aligned on the device.  *dev_base (may
+ * be NULL) receives the device address of host_base.  Registering a range
+ * that overlaps an existing one fails with CLLM_ERR_INVALID_ARG. */
+int cllm_cuda_register_weights(const void* host_base, size_t bytes, void** dev_base);
+
+/* Free the device copy registered for exactly host_base. */
+int cllm_cuda_unregister_weights(const void* host_base);
+
+/* Device address of host_ptr inside a registered range. */
+int cllm_cuda_lookup_weights(const void* host_ptr, const void** dev_ptr);
+
+/* quant.cpp:420-452 — quantize_row_q8_0 over `rows` rows of n floats (device
+ * pointers).  Outputs, per row r: scales[r*n/32 ...] fp32, qs[r*n ...] int8,
+ * bsums[r*n/32 ...] int32.  Bit-exact with the reference on x86, including
+ * NaN inputs (which quantize to -128 there).  n % 32 != 0 fails with
+ * CLLM_ERR_BLOCK_MULTIPLE and "quantize_row_q8_0: n not divisible by 32". */
+int cllm_cuda_quantize_q8_0(const float* x, int64_t n, int rows, float* scales, int8_t* qs,
+                            int32_t* bsums, void* stream);
+
+/* quant.cpp:1374-1475 — matmul_quant (n_rows == 1) and matmul_quant_batch:
+ *   y[t*out_dim + j] = vec_dot_row(W_j, quantize_row_q8_0(x_t)) (+ bias[j])
+ * for t < n_rows, j < out_dim.  W is out_dim rows of (in_dim/block) blocks in
+ * GGML layout.  n_rows <= 0 returns CLLM_OK without touching y
+ * (quant.cpp:1436).  Error strings follow quant.cpp:1379/1443/1370.
+ * By default all pointers are device pointers and the call is asynchronous on
+ * `stream`; the flags above switch x/bias, y and w to host memory.  Scratch
+ * for the quantized activations comes from a per-device workspace that the
+ * library grows on demand (cudaMalloc) and keeps until exit. */
+int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float* bias, int in_dim,
+                           int out_dim, int n_rows, float* y, unsigned flags, void* stream);
+
+/* matmul_quant on activations that are already quantized (the arrays of
+ * QuantizedQ8_0, quant.hpp:118-124, for n_rows rows, device pointers): the
+ * float path of vec_dot_row (quant.cpp:1359-1372) for every weight row.
+ * Lets a caller quantize one activation once and reuse it for several
+ * weight matrices (q/k/v, gate/up).  bias and y are device pointers. */
+int cllm_cuda_matmul_q8(const float* scales, const int8_t* qs, const int32_t* bsums, const void* w,
+                        int type, const float* bias, int in_dim, int out_dim, int n_rows, float* y,
+                        void* stream);
+
+/* Debug / parity entry: the exact int32 partial dot products of every weight
+ * row against every quantized activation row, in the layout
+ *   partials[(t*out_dim + j)*ppr + p],  ppr = in_dim/32 (2*in_dim/32 for Q6_K)
+ * where part p is activation block p (Q6_K: block p/2, half p%2).  Inputs are
+ * device pointers: the quantized activations as cllm_cuda_quantize_q8_0
+ * writes them.  The reference has no counterpart (its vec_dot returns only
+ * the float sum); the values are those its AVX2 kernels form internally. */
+int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim, int out_dim,
+                           int n_rows, int32_t* partials, void* stream);
+
+/* quant.cpp:371-389 (dequantize_block) for the six hot-path types: n values
+ * from the blocks at src (device) into dst (device fp32).  Used by the
+ * engine's embedding lookup (engine.cpp:310-316). */
+int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream);
+
+/* Launch plan cllm_cuda_matmul_quant would use for these arguments (device
+ * weights at w): info[0] kernels launched per call, [1] 1 if the weight tiles
+ * stream through the bulk-copy (TMA) ring, [2] 1 if activation quantization
+ * is fused into the dot kernel, [3] weight rows per tile, [4] warps per row,
+ * [5] pipeline stages, [6] CTAs, [7] dynamic shared memory bytes.  No
+ * counterpart in the reference; used by tests and the benchmark. */
+int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int n_rows, int* info,
+                          int n_info);
+
+/* Read and clear the device-side status word that kernels set when a bounded
+ * wait expires (CLLM_ERR_KERNEL_TIMEOUT); synchronizes the device. */
+int cllm_cuda_check_device_status(void);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated,
+ * truncated to n); returns the length of the full message. */
+int cllm_cuda_last_error(char* buf, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CLLM_CUDA_H */

@@ -1,0 +1,207 @@
+"""GPU parity tests: the CUDA path (through the C ABI) against the oracle.
+
+Bars (from the hot path's contract):
+  * Q8_0 activation quantization: bit-exact (scales, int8 values, block sums);
+  * per-block int32 partial dot products: bit-exact;
+  * row outputs: |y_gpu - y_ref| <= 1e-5 * sum over the row's per-block float
+    terms of |term| (the tree-ordered GPU sum vs the reference's sequential sum).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from cllm_inference_b200 import _lib, synth
+from oracle.oracle import HOT_TYPES, TYPE_NAMES
+from tests import gpu_helpers as G
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-5
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden.npz")
+IDS = [TYPE_NAMES[t] for t in HOT_TYPES]
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_quantize_bit_exact(cuda, lib, oracle):
+    x = synth.make_activations(5, 4096, 11) * np.float32(3.0)
+    x[0, 7] = np.nan
+    x[1, :32] = np.float32(1e-40)
+    x[2, 64] = np.inf
+    x[3, 96:128] = 0.0
+    x[4, 5] = np.float32(-3e38)
+    sc, qs, bs = G.quantize(lib, x)
+    so, qo, bo = oracle.quantize(x)
+    assert np.array_equal(bits(sc), bits(so))
+    assert np.array_equal(qs, qo)
+    assert np.array_equal(bs, bo)
+
+
+SHAPES = [(256, 40, 1), (512, 37, 3), (4096, 300, 1), (4096, 129, 4), (4096, 64, 8), (768, 70, 9),
+          (1024, 33, 2)]
+SHAPES32 = [(96, 50, 2), (32, 9, 1)]
+
+
+def _shapes(t):
+    out = [s for s in SHAPES if s[0] % synth.BLOCK[t] == 0]
+    if synth.BLOCK[t] == 32:
+        out += SHAPES32
+    if t == synth.Q6_K:
+        out.append((14336, 40, 1))
+    return out
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+@pytest.mark.parametrize("misalign", [0, 2], ids=["aligned", "misaligned"])
+def test_partials_bit_exact(cuda, lib, oracle, t, misalign):
+    for k, n, m in _shapes(t):
+        w = synth.make_weights(t, n, k, seed=k * 7 + n + t)
+        x = synth.make_activations(m, k, seed=k + 13 * m)
+        _, qs, _ = oracle.quantize(x)
+        P = G.partials(lib, qs, w, t, k, n, misalign)
+        Po = oracle.partials(w, t, k, n, qs)
+        assert np.array_equal(P, Po), (k, n, m, int(np.sum(P != Po)))
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+@pytest.mark.parametrize("misalign", [0, 2], ids=["aligned", "misaligned"])
+def test_matmul_rows_within_tolerance(cuda, lib, oracle, t, misalign):
+    for k, n, m in _shapes(t):
+        w = synth.make_weights(t, n, k, seed=k * 3 + n + t)
+        x = synth.make_activations(m, k, seed=k + 5 * m)
+        bias = np.random.default_rng(n).standard_normal(n).astype(np.float32) if m == 3 else None
+        y = G.matmul(lib, x, w, t, k, n, bias=bias, misalign=misalign)
+        yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+        G.assert_rows_close(y, yo, ab, REL_TOL, f"{TYPE_NAMES[t]} {k}x{n} m={m}")
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+def test_golden_fixtures(cuda, lib, t):
+    """The committed vectors produced by the reference build itself."""
+    g = np.load(GOLDEN)
+    for case in ("seeded", "odd", "reftest", "special"):
+        key = f"{TYPE_NAMES[t]}/{case}"
+        k, n, m, tt = (int(v) for v in g[key + "/shape"])
+        x, w = g[key + "/x"], g[key + "/w"]
+        bias = g[key + "/bias"]
+        bias = bias if bias.size else None
+        sc, qs, bs = G.quantize(lib, x)
+        assert np.array_equal(bits(sc), bits(g[key + "/scales"])), key
+        assert np.array_equal(qs, g[key + "/qs"]), key
+        assert np.array_equal(bs, g[key + "/bsums"]), key
+        from oracle.oracle import Oracle
+        _, ab = Oracle().matmul(x, w, tt, k, n, bias=bias, with_abs=True)
+        for mis in (0, 2):
+            y = G.matmul(lib, x, w, tt, k, n, bias=bias, misalign=mis)
+            G.assert_rows_close(y, g[key + "/y"], ab, REL_TOL, key)
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+def test_nan_activation_sign_trick(cuda, lib, oracle, t):
+    """A NaN activation quantizes to -128; the reference's AVX2 Q8_0/Q6_K dots
+    then form the sign-trick product, which the GPU reproduces exactly."""
+    k, n = 512, 64
+    w = synth.make_weights(t, n, k, seed=99)
+    x = synth.make_activations(2, k, 3)
+    x[0, [1, 2, 50, 300, 301]] = np.nan
+    _, qs, _ = oracle.quantize(x)
+    assert (qs == -128).sum() == 5
+    assert np.array_equal(G.partials(lib, qs, w, t, k, n), oracle.partials(w, t, k, n, qs))
+    y = G.matmul(lib, x, w, t, k, n)
+    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+    assert np.all(np.isfinite(yo))
+    G.assert_rows_close(y, yo, ab, REL_TOL, "nan rows")
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+def test_matmul_q8_prequantized(cuda, lib, oracle, t):
+    k, n, m = 1024, 77, 3
+    w = synth.make_weights(t, n, k, seed=5)
+    x = synth.make_activations(m, k, 6)
+    x[1, 9] = np.nan
+    sc, qs, bs = oracle.quantize(x)
+    bias = np.arange(n, dtype=np.float32)
+    y = G.matmul_q8(lib, sc, qs, bs, w, t, k, n, bias=bias)
+    yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+    G.assert_rows_close(y, yo, ab, REL_TOL, "matmul_q8")
+
+
+@pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
+def test_dequantize_bit_exact(cuda, lib, oracle, t):
+    nrow, k = 9, 512
+    w = synth.make_weights(t, nrow, k, seed=8)
+    _, wp = G.dev_bytes(w)
+    out = torch.empty(nrow * k, dtype=torch.float32, device="cuda")
+    _lib.check(lib.cllm_cuda_dequantize(wp, t, nrow * k, G.dptr(out), G.stream()))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(out.cpu().numpy()), bits(oracle.dequantize(w, t, nrow * k)))
+
+
+def test_host_io_and_registry(cuda, lib, oracle):
+    """matmul_quant with host x/bias/y and a host weight pointer resolved through
+    the registry (the path the quant.hpp shim uses)."""
+    import ctypes
+
+    t, k, n, m = synth.Q4_K, 4096, 500, 3
+    w = synth.make_weights(t, n, k, seed=21)
+    x = synth.make_activations(m, k, 22)
+    bias = np.linspace(-1, 1, n, dtype=np.float32)
+    y = np.full((m, n), np.nan, np.float32)
+    base = w.ctypes.data
+    dev = ctypes.c_void_p()
+    _lib.check(lib.cllm_cuda_register_weights(ctypes.c_void_p(base), w.nbytes, ctypes.byref(dev)))
+    try:
+        assert (dev.value - base) % 256 == 0, "device copy keeps the host offset modulo 256"
+        _lib.check(lib.cllm_cuda_matmul_quant(x.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(base), t,
+                                              bias.ctypes.data_as(ctypes.c_void_p), k, n, m,
+                                              y.ctypes.data_as(ctypes.c_void_p),
+                                              _lib.HOST_IO | _lib.W_HOST, None))
+        yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+        G.assert_rows_close(y, yo, ab, REL_TOL, "host io")
+        # a pointer past the range is rejected
+        assert lib.cllm_cuda_matmul_quant(x.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(base + 144), t,
+                                          None, k, n, m, y.ctypes.data_as(ctypes.c_void_p),
+                                          _lib.HOST_IO | _lib.W_HOST, None) == _lib.ERR_INVALID_ARG
+        assert lib.cllm_cuda_register_weights(ctypes.c_void_p(base + 100), 10, None) == _lib.ERR_INVALID_ARG
+    finally:
+        _lib.check(lib.cllm_cuda_unregister_weights(ctypes.c_void_p(base)))
+    assert lib.cllm_cuda_matmul_quant(x.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(base), t, None, k, n,
+                                      m, y.ctypes.data_as(ctypes.c_void_p), _lib.HOST_IO | _lib.W_HOST,
+                                      None) == _lib.ERR_NOT_REGISTERED
+
+
+def test_empty_and_degenerate(cuda, lib, oracle):
+    t = synth.Q4_K
+    w = synth.make_weights(t, 8, 256, 1)
+    # in_dim == 0: every row is just the bias (quant.cpp: empty dot)
+    bias = np.arange(8, dtype=np.float32)
+    y = G.matmul(lib, np.zeros((2, 0), np.float32), np.zeros(0, np.uint8), t, 0, 8, bias=bias)
+    assert np.array_equal(y, np.stack([bias, bias]))
+    # all-zero activations: d = 0, id = 0, every q = 0
+    y = G.matmul(lib, np.zeros((1, 256), np.float32), w, t, 256, 8)
+    assert np.array_equal(y, np.zeros((1, 8), np.float32))
+
+
+# the 8B decode layer shapes at M=1 and M=4, and the extra Q8_0 / Q5_K pass.
+LAYER_SHAPES = [("q/o", synth.Q4_K, 4096, 4096), ("k/v", synth.Q4_K, 4096, 1024),
+                ("gate/up", synth.Q4_K, 4096, 14336), ("down", synth.Q6_K, 14336, 4096),
+                ("lm_head", synth.Q6_K, 4096, 128256), ("q8_0", synth.Q8_0, 4096, 4096),
+                ("q5_k", synth.Q5_K, 4096, 4096)]
+
+
+@pytest.mark.parametrize("name,t,k,n", LAYER_SHAPES, ids=[s[0] for s in LAYER_SHAPES])
+def test_baseline_layer_shapes(cuda, lib, oracle, name, t, k, n):
+    w = synth.make_weights(t, n, k, seed=n + k + t)
+    x = synth.make_activations(4, k, seed=k)
+    y4 = G.matmul(lib, x, w, t, k, n)
+    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+    worst = G.assert_rows_close(y4, yo, ab, REL_TOL, name)
+    assert worst < 1.0
+    # size-independent properties: M=4 rows equal four M=1 calls bit for bit, and reruns are deterministic
+    for r in range(4):
+        y1 = G.matmul(lib, x[r:r + 1], w, t, k, n)
+        assert np.array_equal(bits(y1[0]), bits(y4[r]))
+    assert np.array_equal(bits(G.matmul(lib, x, w, t, k, n)), bits(y4))
