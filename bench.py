@@ -227,10 +227,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-shape, prefill and e2e passes")
+    ap.add_argument("--shape", default=None,
+                    help="profiling case TYPE:K:N:M (e.g. Q4_K:4096:14336:1): run only that matmul_quant "
+                         "--steps times after --warmup, and print its timing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.shape:
+        return run_shape(args)
 
     import torch
 
@@ -255,6 +260,9 @@ def main():
     stream = torch.cuda.current_stream()
     sp = ctypes.c_void_p(stream.cuda_stream)
 
+    def cur_stream():
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
     def barrier():
         if dist is not None:
             dist.barrier()
@@ -268,16 +276,21 @@ def main():
     calls = sweep_calls()
     step_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
 
-    def run_call(l, name, t, k, n, m=1):
+    def run_call(l, name, t, k, n, m=1, st=None):
         w = weights[(l, name)]
         return lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xs[k].data_ptr()), ctypes.c_void_p(w.data_ptr()), t,
-                                          None, k, n, m, ctypes.c_void_p(ys[n].data_ptr()), 0, sp)
+                                          None, k, n, m, ctypes.c_void_p(ys[n].data_ptr()), 0,
+                                          st if st is not None else cur_stream())
 
-    def step(m=1):
-        for c in calls:
-            rc = run_call(*c, m=m)
+    def run_calls(cs, m=1):
+        st = cur_stream()
+        for c in cs:
+            rc = run_call(*c, m=m, st=st)
             if rc:
                 _lib.check(rc)
+
+    def step(m=1):
+        run_calls(calls, m)
 
     launches_per_step = 0
     info = (ctypes.c_int * 8)()
@@ -289,8 +302,11 @@ def main():
                                          14336, 1, info, 8))
     plan_q4k = list(info)
 
+    # The sweep's 225 launches are captured once in a CUDA graph and replayed
+    # per step, so the timed region measures the GPU, not Python launch cost.
+    graph = capture_graph(torch, step)
     for _ in range(args.warmup):
-        step()
+        graph.replay()
     torch.cuda.synchronize()
     _lib.check(lib.cllm_cuda_check_device_status())
 
@@ -301,7 +317,7 @@ def main():
         torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            graph.replay()
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -314,23 +330,20 @@ def main():
     value = world * step_bytes * args.steps / (ms_total * 1e-3) / 1e9
     _lib.check(lib.cllm_cuda_check_device_status())
 
-    # ---- roofline of the dominant kernel: the Q4_K GEMV launches, each bracketed by events
+    # ---- roofline of the dominant kernel: the 192 Q4_K GEMV launches of a
+    # step, captured in their own graph and replayed `steps` times between
+    # events; average launch duration = elapsed / launches.
     q4 = [c for c in calls if c[2] == synth.Q4_K]
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(len(q4) * args.steps)]
-    i = 0
+    g4 = capture_graph(torch, lambda: run_calls(q4))
+    g4.replay()
+    a4, b4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    a4.record(stream)
     for _ in range(args.steps):
-        for c in calls:
-            if c[2] == synth.Q4_K:
-                evs[i][0].record(stream)
-                _lib.check(run_call(*c))
-                evs[i][1].record(stream)
-                i += 1
-            else:
-                _lib.check(run_call(*c))
+        g4.replay()
+    b4.record(stream)
     torch.cuda.synchronize()
-    q4_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    q4_ms = a4.elapsed_time(b4) / (args.steps * len(q4))
     q4_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in q4) / len(q4)
     peak, peak_kind = measured_peaks()
     achieved = q4_bytes / (q4_ms * 1e-3) / 1e9
@@ -374,19 +387,79 @@ def main():
     return 0
 
 
+def run_shape(args):
+    """One matmul_quant shape, eager launches (used for ncu captures of a single kernel)."""
+    import torch
+
+    from cllm_inference_b200 import _lib
+
+    tname, k, n, m = args.shape.split(":")
+    t, k, n, m = synth.BY_NAME[tname], int(k), int(n), int(m)
+    torch.cuda.set_device(0)
+    lib = _lib.load()
+    _lib.check(lib.cllm_cuda_init(0))
+    w = synth.make_weights_torch(t, n, k, seed=1, device="cuda")
+    x = torch.from_numpy(synth.make_activations(m, k, 2)).cuda()
+    y = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def go():
+        _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()), t,
+                                              None, k, n, m, ctypes.c_void_p(y.data_ptr()), 0, st))
+    for _ in range(args.warmup):
+        go()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        go()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    info = (ctypes.c_int * 8)()
+    _lib.check(lib.cllm_cuda_matmul_plan(ctypes.c_void_p(w.data_ptr()), t, k, n, m, info, 8))
+    print(json.dumps({"shape": args.shape, "ms": round(ms, 4), "gbs": round(call_bytes(t, k, n, m) / (ms * 1e-3) / 1e9, 1),
+                      "bytes": call_bytes(t, k, n, m), "plan": list(info),
+                      "note": "eager back-to-back launches (includes launch gaps)"}))
+    return 0
+
+
+def capture_graph(torch, fn):
+    """Run fn once on a side stream (warm-up), then capture it in a CUDA graph."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
 def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_call, calls, args):
     out = {}
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def timed(fn, reps=1):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        flush.random_(0, 255)
-        a.record(stream)
-        for _ in range(reps):
-            fn()
-        b.record(stream)
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / reps
+        """fn (graph-captured) after an L2 flush, between events."""
+        g = capture_graph(torch, fn)
+        best = None
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            flush.random_(0, 255)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+        return best
+
+    def cur():
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     # per shape: the 32 distinct copies of a layer matrix in a row, after an L2 flush
     per = {}
@@ -394,27 +467,22 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
     for m in (1, 4):
         for label, name in shapes:
             (_, t, k, n) = next(p for p in LAYER if p[0] == name)
-            for _ in range(2):
-                for l in range(N_LAYERS):
-                    _lib.check(run_call(l, name, t, k, n, m))
-            ms = min(timed(lambda: [_lib.check(run_call(l, name, t, k, n, m)) for l in range(N_LAYERS)])
-                     for _ in range(3))
+            ms = timed(lambda: [_lib.check(run_call(l, name, t, k, n, m, st=cur())) for l in range(N_LAYERS)])
             per[f"{label} {synth.NAMES[t]} {n}x{k} M={m}"] = round(
                 N_LAYERS * call_bytes(t, k, n, m) / (ms * 1e-3) / 1e9, 1)
-        _lib.check(run_call(0, "lm_head", synth.Q6_K, 4096, 128256, m))
-        ms = min(timed(lambda: _lib.check(run_call(0, "lm_head", synth.Q6_K, 4096, 128256, m))) for _ in range(3))
+        ms = timed(lambda: _lib.check(run_call(0, "lm_head", synth.Q6_K, 4096, 128256, m, st=cur())))
         per[f"lm_head Q6_K 128256x4096 M={m}"] = round(call_bytes(synth.Q6_K, 4096, 128256, m) / (ms * 1e-3) / 1e9, 1)
     # extra pass: Q8_0 and Q5_K 4096x4096 (32 distinct copies each)
     for t in (synth.Q8_0, synth.Q5_K):
         ws = [synth.make_weights_torch(t, 4096, 4096, seed=77 + l, device=dev) for l in range(N_LAYERS)]
         for m in (1, 4):
             def go():
+                st = cur()
                 for w in ws:
                     _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xs[4096].data_ptr()),
                                                           ctypes.c_void_p(w.data_ptr()), t, None, 4096, 4096, m,
-                                                          ctypes.c_void_p(ys[4096].data_ptr()), 0, sp))
-            go()
-            ms = min(timed(go) for _ in range(3))
+                                                          ctypes.c_void_p(ys[4096].data_ptr()), 0, st))
+            ms = timed(go)
             per[f"{synth.NAMES[t]} 4096x4096 M={m}"] = round(
                 N_LAYERS * call_bytes(t, 4096, 4096, m) / (ms * 1e-3) / 1e9, 1)
         del ws
@@ -430,9 +498,8 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
         def go():
             _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
                                                   synth.Q4_K, None, 4096, 14336, M, ctypes.c_void_p(y.data_ptr()),
-                                                  0, sp))
-        go()
-        ms = min(timed(go) for _ in range(2))
+                                                  0, cur()))
+        ms = timed(go)
         pre[f"M={M}"] = {"ms": round(ms, 3), "tok_s": round(M / (ms * 1e-3), 1),
                          "tops": round(2.0 * M * 14336 * 4096 / (ms * 1e-3) / 1e12, 2)}
     out["prefill_14336x4096_q4k"] = pre

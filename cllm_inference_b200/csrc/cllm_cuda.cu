@@ -196,7 +196,8 @@ struct GemvPlan {
 // Tile / pipeline choice.  want_fused: quantize the activations inside the
 // kernel when they fit (m rows of K).
 GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, int m, bool want_fused,
-                   const DeviceInfo& di) {
+                   const DeviceInfo& di, const float* x = nullptr) {
+    if (x && (reinterpret_cast<uintptr_t>(x) & 15) != 0) want_fused = false;  // fused loads are float4
     GemvPlan pl{};
     const int upr = units_per_row(type, K);
     const int max_wpr = std::max(1, std::min(kGemvWarps, upr / 32));
@@ -232,14 +233,46 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
     return pl;
 }
 
+// Raise a kernel's dynamic shared-memory limit to the device maximum once
+// (per device); the launch's own size still decides occupancy.
+int opt_in_smem(const void* fn, int dev) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, bool> done;
+    std::lock_guard<std::mutex> lk(mu);
+    auto key = std::make_pair(fn, dev);
+    if (done.count(key)) return CLLM_OK;
+    CLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)g_dev[dev].max_smem_optin));
+    done[key] = true;
+    return CLLM_OK;
+}
+
 int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams& p, cudaStream_t st) {
     GemvFn fn = select_gemv(type, pl.tma, pl.fused, emit, m);
     if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no kernel for type %d, %d rows", type, m);
-    if (pl.tma) {
-        CLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)pl.smem));
+    if (pl.smem > 48 * 1024) {
+        int dev;
+        CLLM_CUDA_TRY(cudaGetDevice(&dev));
+        if (int rc = opt_in_smem(reinterpret_cast<const void*>(fn), dev)) return rc;
     }
-    fn<<<pl.grid, kGemvThreads, pl.smem, st>>>(p);
+    if (pl.tma) {
+        // Programmatic dependent launch: the kernel may begin (barrier set-up,
+        // weight prefetch) while its predecessor in the stream finishes; it
+        // reads activations only after griddepcontrol.wait.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(pl.grid);
+        cfg.blockDim = dim3(kGemvThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, p));
+    } else {
+        fn<<<pl.grid, kGemvThreads, pl.smem, st>>>(p);
+    }
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }
@@ -435,7 +468,7 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
 
     for (int t0 = 0; t0 < n_rows; t0 += 8) {
         const int m = std::min(8, n_rows - t0);
-        const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di);
+        const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di, xd + (size_t)t0 * in_dim);
         GemvParams p{};
         p.w = wd;
         p.row_bytes = row_bytes;

@@ -121,22 +121,74 @@ struct ActGmem {
     __device__ __forceinline__ int2 bs2(int t, int b) const {
         return __ldg(reinterpret_cast<const int2*>(bs + (int64_t)t * nb + b));
     }
+    // Q6_K unit: scales of blocks b and b + 2
+    __device__ __forceinline__ float2 dx_q6(int t, int b) const { return make_float2(dx1(t, b), dx1(t, b + 2)); }
 };
 
 // Quantized activations in this CTA's shared memory (fused quantization).
+//
+// Layout, chosen so that the lane access pattern of every unit map is free of
+// shared-memory bank conflicts:
+//   * block order: activation block b is stored at position perm(b).  For
+//     Q6_K, whose unit pairs sub-blocks p and p+2 of a 128-value group,
+//     sub-blocks (0,1,2,3) of each group are stored as (0,2,1,3), so a unit's
+//     two blocks are adjacent; every other type keeps b.
+//   * row stride kp = K rounded up to 128 bytes;
+//   * 16-byte slot swizzle inside each 128-byte line: slot ^= (slot >> 3) & 7.
+// Lane u of a warp reads 64 contiguous logical bytes (or 32 for the
+// 32-value types); with the swizzle the eight lanes of each quarter-warp hit
+// eight different 16-byte bank groups.
+template <int TYPE>
+__host__ __device__ __forceinline__ int act_perm(int b) {
+    if constexpr (TYPE == kQ6_K) {
+        const int sub = b & 3;
+        return (b & ~3) | ((sub & 1) << 1) | (sub >> 1);
+    } else {
+        return b;
+    }
+}
+
+__host__ __device__ __forceinline__ uint32_t act_swizzle(uint32_t off) {
+    const uint32_t slot = off >> 4;
+    return ((slot ^ ((slot >> 3) & 7u)) << 4) | (off & 15u);
+}
+
+__host__ __device__ __forceinline__ int act_row_stride(int K) { return (K + 127) & ~127; }
+
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+
+template <int TYPE>
 struct ActSmem {
-    uint32_t qx, dx, bs;  // shared addresses: [M][K] int8, [M][nb] f32, [M][nb] i32
-    int K, nb;
+    uint32_t qx, dx, bs;  // shared addresses: [M][kp] int8 (swizzled), [M][nb] f32, [M][nb] i32
+    int kp, nb;
     __device__ __forceinline__ void x32(int t, int b, int (&x)[8]) const {
-        const uint32_t a = qx + (uint32_t)(t * K + 32 * b);
-        const uint4 v0 = lds128(a), v1 = lds128(a + 16);
+        const uint32_t row = qx + (uint32_t)(t * kp);
+        const uint32_t off = 32u * (uint32_t)act_perm<TYPE>(b);
+        const uint4 v0 = lds128(row + act_swizzle(off)), v1 = lds128(row + act_swizzle(off + 16));
         x[0] = (int)v0.x; x[1] = (int)v0.y; x[2] = (int)v0.z; x[3] = (int)v0.w;
         x[4] = (int)v1.x; x[5] = (int)v1.y; x[6] = (int)v1.z; x[7] = (int)v1.w;
     }
-    __device__ __forceinline__ float dx1(int t, int b) const { return __uint_as_float(lds32(dx + 4u * (t * nb + b))); }
-    __device__ __forceinline__ int bs1(int t, int b) const { return (int)lds32(bs + 4u * (t * nb + b)); }
-    __device__ __forceinline__ float2 dx2(int t, int b) const { return make_float2(dx1(t, b), dx1(t, b + 1)); }
-    __device__ __forceinline__ int2 bs2(int t, int b) const { return make_int2(bs1(t, b), bs1(t, b + 1)); }
+    __device__ __forceinline__ float dx1(int t, int b) const {
+        return __uint_as_float(lds32(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b))));
+    }
+    __device__ __forceinline__ int bs1(int t, int b) const {
+        return (int)lds32(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+    }
+    // blocks b and its unit partner, stored adjacently (perm(b) even)
+    __device__ __forceinline__ float2 dx2(int t, int b) const {
+        const uint2 v = lds64(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+        return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+    }
+    __device__ __forceinline__ int2 bs2(int t, int b) const {
+        const uint2 v = lds64(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+        return make_int2((int)v.x, (int)v.y);
+    }
+    // Q6_K unit: scales of blocks b and b + 2, adjacent after the permutation
+    __device__ __forceinline__ float2 dx_q6(int t, int b) const { return dx2(t, b); }
 };
 
 template <int TYPE, int M, bool EMIT, int ALIGN, class Src, class Act>
@@ -224,11 +276,22 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
         const int sha = 16 * pr;
         const float sA0 = (float)(int)(int8_t)(SC[0] >> sha), sA1 = (float)(int)(int8_t)(SC[0] >> (sha + 8));
         const float sB0 = (float)(int)(int8_t)(SC[1] >> sha), sB1 = (float)(int)(int8_t)(SC[1] >> (sha + 8));
+        // six-bit quants v in [0,63] per byte; the weight is v - 32
+        uint32_t va[8], vb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            va[i] = (L[i] & 0x0F0F0F0Fu) | ((H[i] << (4 - 2 * pr)) & 0x30303030u);
+            vb[i] = ((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> (2 * pr)) & 0x30303030u);
+        }
+        // Few activation rows: form sum(v*x) and subtract 32*sum(x) per half
+        // (four dp4a per half) instead of re-biasing every weight byte; the
+        // integers are identical.  More rows: re-bias the weights once.
+        constexpr bool kOffset = M <= 2;
         int qa[8], qb[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            qa[i] = q6_to_s8((L[i] & 0x0F0F0F0Fu) | ((H[i] << (4 - 2 * pr)) & 0x30303030u));
-            qb[i] = q6_to_s8(((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> (2 * pr)) & 0x30303030u));
+            qa[i] = kOffset ? (int)va[i] : q6_to_s8(va[i]);
+            qb[i] = kOffset ? (int)vb[i] : q6_to_s8(vb[i]);
         }
         const int bA = 8 * s + 4 * g + pr, bB = bA + 2;
 #pragma unroll
@@ -244,23 +307,34 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
                 PB0 = dp4a(qb[i], xb[i], PB0);
                 PB1 = dp4a(qb[i + 4], xb[i + 4], PB1);
             }
+            if constexpr (kOffset) {
+                int hA0 = 0, hA1 = 0, hB0 = 0, hB1 = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    hA0 = dp4a(xa[i], 0x20202020, hA0);
+                    hA1 = dp4a(xa[i + 4], 0x20202020, hA1);
+                    hB0 = dp4a(xb[i], 0x20202020, hB0);
+                    hB1 = dp4a(xb[i + 4], 0x20202020, hB1);
+                }
+                PA0 -= hA0; PA1 -= hA1; PB0 -= hB0; PB1 -= hB1;
+            }
             if ((quirk >> t) & 1u) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    PA0 += signtrick_fix(qa[i], xa[i]);
-                    PA1 += signtrick_fix(qa[i + 4], xa[i + 4]);
-                    PB0 += signtrick_fix(qb[i], xb[i]);
-                    PB1 += signtrick_fix(qb[i + 4], xb[i + 4]);
+                    PA0 += signtrick_fix(q6_to_s8(va[i]), xa[i]);
+                    PA1 += signtrick_fix(q6_to_s8(va[i + 4]), xa[i + 4]);
+                    PB0 += signtrick_fix(q6_to_s8(vb[i]), xb[i]);
+                    PB1 += signtrick_fix(q6_to_s8(vb[i + 4]), xb[i + 4]);
                 }
             }
             if constexpr (EMIT) {
                 prow[2 * bA] = PA0; prow[2 * bA + 1] = PA1;
                 prow[2 * bB] = PB0; prow[2 * bB + 1] = PB1;
             }
-            const float dxA = act.dx1(t, bA), dxB = act.dx1(t, bB);
+            const float2 dxAB = act.dx_q6(t, bA);
             // sc*P products are exact integers below 2^24, as in the reference
-            acc[t] = fmaf(d * dxA, sA0 * i2f_exact(PA0) + sA1 * i2f_exact(PA1), acc[t]);
-            acc[t] = fmaf(d * dxB, sB0 * i2f_exact(PB0) + sB1 * i2f_exact(PB1), acc[t]);
+            acc[t] = fmaf(d * dxAB.x, sA0 * i2f_exact(PA0) + sA1 * i2f_exact(PA1), acc[t]);
+            acc[t] = fmaf(d * dxAB.y, sB0 * i2f_exact(PB0) + sB1 * i2f_exact(PB1), acc[t]);
         }
     } else if constexpr (TYPE == kQ8_0) {
         const int b = u;
@@ -401,37 +475,71 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
 }
 
 // Quantize x [M][K] into this CTA's shared memory (quantize_row_q8_0,
-// quant.cpp:420-452, the same per-warp code as quantize_q8_0_kernel).
+// quant.cpp:420-452, the same IEEE steps as quantize_q8_0_kernel).  Eight
+// lanes share a 32-value block, one float4 each; every thread issues the
+// loads of four blocks before reducing them, so the prologue costs about one
+// L2 round trip per four blocks per group.  x must be 16-byte aligned.
 // Returns the per-row "holds -128" mask.  Called by all threads.
-template <int M>
+template <int M, int TYPE>
 __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
                                                      uint8_t* qs, float* dx, int* bs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kp = act_row_stride(K);
+    constexpr int kGroups = kGemvThreads / 8;  // 32 blocks in flight per pass
+    constexpr int kUnroll = 4;
+    const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
     const int nb = K >> 5;
+    const int total = M * nb;
     uint32_t mask = 0;
-    for (int blk = warp; blk < M * nb; blk += kGemvWarps) {
-        const int t = blk / nb, b = blk - t * nb;
-        const float v = __ldg(x + (int64_t)t * K + 32 * b + lane);
-        const float a = fabsf(v);
-        float amax = (a > 0.0f) ? a : 0.0f;
+    for (int base = 0; base < total; base += kGroups * kUnroll) {
+        float4 v[kUnroll];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-        const float d = amax / 127.0f;
-        const float id = (d != 0.0f) ? 1.0f / d : 0.0f;
-        const float r = rintf(v * id);
-        int q = (r >= -2147483648.0f && r < 2147483648.0f) ? (int)r : INT32_MIN;
-        q = q > 127 ? 127 : (q < -128 ? -128 : q);
-        qs[t * K + 32 * b + lane] = (uint8_t)(int8_t)q;
-        int sum = q;
+        for (int u = 0; u < kUnroll; ++u) {
+            const int blk = base + g + kGroups * u;
+            if (blk < total) {
+                const int t = blk / nb, b = blk - t * nb;
+                v[u] = __ldg(reinterpret_cast<const float4*>(x + (int64_t)t * K + 32 * b + 4 * sub));
+            } else {
+                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-        if (__any_sync(0xFFFFFFFFu, q == -128)) mask |= 1u << t;
-        if (lane == 0) {
-            dx[t * nb + b] = d;
-            bs[t * nb + b] = sum;
+        for (int u = 0; u < kUnroll; ++u) {
+            const int blk = base + g + kGroups * u;  // uniform within each 8-lane group
+            const float a0 = fabsf(v[u].x), a1 = fabsf(v[u].y), a2 = fabsf(v[u].z), a3 = fabsf(v[u].w);
+            // max over non-NaN values, as `if (a > amax) amax = a` from 0
+            float amax = (a0 > 0.0f) ? a0 : 0.0f;
+            amax = (a1 > amax) ? a1 : amax;
+            amax = (a2 > amax) ? a2 : amax;
+            amax = (a3 > amax) ? a3 : amax;
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            const float d = amax / 127.0f;
+            const float id = (d != 0.0f) ? 1.0f / d : 0.0f;
+            int q[4];
+            const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float r = rintf(vv[e] * id);
+                int qi = (r >= -2147483648.0f && r < 2147483648.0f) ? (int)r : INT32_MIN;
+                q[e] = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
+            }
+            int sum = q[0] + q[1] + q[2] + q[3];
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+            if (blk < total) {
+                const int t = blk / nb, b = blk - t * nb;
+                const uint32_t packed = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) |
+                                        ((uint32_t)(q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+                const int pb = act_perm<TYPE>(b);
+                *reinterpret_cast<uint32_t*>(qs + t * kp + act_swizzle(32u * pb + 4u * sub)) = packed;
+                if ((q[0] == -128) | (q[1] == -128) | (q[2] == -128) | (q[3] == -128)) mask |= 1u << t;
+                if (sub == 0) {
+                    dx[t * nb + pb] = d;
+                    bs[t * nb + pb] = sum;
+                }
+            }
         }
     }
-    // every thread of a warp holds the same mask; OR across warps
     uint32_t all = 0;
 #pragma unroll
     for (int t = 0; t < M; ++t)
@@ -442,7 +550,7 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
 // Shared-memory bytes the fused quantization needs for M rows of K.
 __host__ __device__ inline uint32_t fused_act_bytes(int M, int K) {
     const uint32_t nb = (uint32_t)K / 32u;
-    return ((uint32_t)(M * K) + 15u) / 16u * 16u + 8u * (uint32_t)M * nb;
+    return (uint32_t)(M * act_row_stride(K)) + 8u * (uint32_t)M * nb;
 }
 
 template <int TYPE, int M, bool EMIT, bool FUSED>
@@ -479,19 +587,26 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_tma_kernel(const GemvPar
         }
     }
 
+    // Programmatic dependent launch: the next kernel in the stream may start
+    // its own prologue (barrier set-up, weight prefetch) while this one runs;
+    // the activations, which a previous kernel may produce, are read only
+    // after griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
     // Activations: quantized here while the first weight tiles stream in, or
     // read from the global workspace.
     uint32_t quirk;
-    ActSmem as{};
+    ActSmem<TYPE> as{};
     ActGmem ag{p.qx, p.dx, p.bs, p.K, nb};
     if constexpr (FUSED) {
         uint8_t* qs = smem + kGemvSmemHeader;
-        const uint32_t qbytes = ((uint32_t)(M * p.K) + 15u) / 16u * 16u;
+        const uint32_t qbytes = (uint32_t)(M * act_row_stride(p.K));
         float* dxs = reinterpret_cast<float*>(qs + qbytes);
         int* bss = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
-        const uint32_t qm = quantize_to_smem<M>(p.x, p.K, qs, dxs, bss);
+        const uint32_t qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss);
         quirk = (TYPE == kQ8_0 || TYPE == kQ6_K) ? qm : 0u;
-        as = ActSmem{smem_addr(qs), smem_addr(dxs), smem_addr(bss), p.K, nb};
+        as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), act_row_stride(p.K), nb};
     } else {
         quirk = gemv_quirk_mask<TYPE, M>(p);
     }
