@@ -261,7 +261,7 @@ int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams
         // reads activations only after griddepcontrol.wait.
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(pl.grid);
-        cfg.blockDim = dim3(kGemvThreads);
+        cfg.blockDim = dim3(kTmaThreads);
         cfg.dynamicSmemBytes = pl.smem;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];

@@ -166,6 +166,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     }
 }
 
+// Wait with the same bound, returning early once another thread of the CTA
+// has set *abort (and setting it when this wait expires).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(&g_device_status, kStatusTimeout);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Barrier over the first `threads` threads of the CTA (named barrier 1).
+__device__ __forceinline__ void named_barrier_sync(int threads) {
+    asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
 // ---- misc -----------------------------------------------------------------
 template <int M>
 __device__ __forceinline__ void warp_sum(float (&v)[M]) {

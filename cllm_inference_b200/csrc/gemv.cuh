@@ -42,9 +42,18 @@ struct GemvParams {
     uint32_t stage_bytes;
 };
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kGemvSmemHeader = 1024;  // mbarriers + reduction scratch, before the stage ring
+constexpr int kGemvWarps = 8;                      // warps that compute (R rows x wpr warps per row)
+constexpr int kGemvThreads = kGemvWarps * 32;      // direct-load kernel, quantize kernel
+constexpr int kTmaThreads = kGemvThreads + 32;     // + one producer warp that streams the weight tiles
+constexpr int kGemvSmemHeader = 4096;              // barriers, flags, per-stage partial sums, before the ring
+
+// Layout of the TMA kernel's shared-memory header.
+constexpr int kHdrFull = 0;        // 8 x u64: "stage holds its tile" (tx-count barriers)
+constexpr int kHdrEmpty = 64;      // 8 x u64: "every compute warp is done with the stage"
+constexpr int kHdrAbort = 128;     // int: a bounded wait expired
+constexpr int kHdrQuirk = 132;     // u32: per-row "activation holds -128" bits
+constexpr int kHdrCount = 256;     // 8 stages x 8 rows of int: warps of a row that finished the tile
+constexpr int kHdrRed = 512;       // 8 stages x 8 warps x 8 floats: partial row sums
 
 template <int T> struct TypeInfo;
 template <> struct TypeInfo<kQ4_0> { static constexpr int kBlock = 32, kBytes = 18, kUnitsPerBlock = 1; };
@@ -105,6 +114,14 @@ __device__ __forceinline__ uint32_t spread4_to_bit4(uint32_t h) {
     return (((h & 0xFu) * 0x00204081u) & 0x01010101u) << 4;
 }
 
+// Q6_K lane order: unit v -> (super-block, group, pair).  The units of the
+// even super-blocks come first, so a warp's 32 lanes mostly share one
+// super-block parity, and with it the 2-byte misalignment of a 210-byte
+// super-block inside a 16-byte-aligned row.
+__device__ __forceinline__ int q6k_superblock_of(int v, int se) {
+    return v < 4 * se ? 2 * (v >> 2) : 2 * ((v - 4 * se) >> 2) + 1;
+}
+
 // Quantized activations in global memory (written by quantize_q8_0_kernel or
 // passed in by the caller).
 struct ActGmem {
@@ -139,11 +156,18 @@ struct ActGmem {
 // 32-value types); with the swizzle the eight lanes of each quarter-warp hit
 // eight different 16-byte bank groups.
 template <int TYPE>
-__host__ __device__ __forceinline__ int act_perm(int b) {
+__host__ __device__ __forceinline__ int act_perm(int b, int nb) {
     if constexpr (TYPE == kQ6_K) {
-        const int sub = b & 3;
-        return (b & ~3) | ((sub & 1) << 1) | (sub >> 1);
+        // Q6_K units are numbered in "lane order" v: the units of the even
+        // super-blocks first, then those of the odd ones (see q6k_unit_of),
+        // and unit v keeps its two blocks (sub-blocks pr and pr+2 of group g)
+        // at positions 2v and 2v+1.
+        const int sb = b >> 3, g = (b >> 2) & 1, sub = b & 3;
+        const int se = ((nb >> 3) + 1) >> 1;  // number of even super-blocks
+        const int vbase = (sb & 1) ? 4 * se + 4 * (sb >> 1) : 4 * (sb >> 1);
+        return 2 * (vbase + 2 * g + (sub & 1)) + (sub >> 1);
     } else {
+        (void)nb;
         return b;
     }
 }
@@ -163,28 +187,29 @@ __device__ __forceinline__ uint2 lds64(uint32_t a) {
 
 template <int TYPE>
 struct ActSmem {
-    uint32_t qx, dx, bs;  // shared addresses: [M][kp] int8 (swizzled), [M][nb] f32, [M][nb] i32
+    uint32_t qx, dx, bs, hs;  // shared addresses: [M][kp] int8 (swizzled), [M][nb] f32, [M][nb] i32,
+                              // [M][nb] int2 = 32 x (sum of q over each 16-value half)
     int kp, nb;
     __device__ __forceinline__ void x32(int t, int b, int (&x)[8]) const {
         const uint32_t row = qx + (uint32_t)(t * kp);
-        const uint32_t off = 32u * (uint32_t)act_perm<TYPE>(b);
+        const uint32_t off = 32u * (uint32_t)act_perm<TYPE>(b, nb);
         const uint4 v0 = lds128(row + act_swizzle(off)), v1 = lds128(row + act_swizzle(off + 16));
         x[0] = (int)v0.x; x[1] = (int)v0.y; x[2] = (int)v0.z; x[3] = (int)v0.w;
         x[4] = (int)v1.x; x[5] = (int)v1.y; x[6] = (int)v1.z; x[7] = (int)v1.w;
     }
     __device__ __forceinline__ float dx1(int t, int b) const {
-        return __uint_as_float(lds32(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b))));
+        return __uint_as_float(lds32(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b, nb))));
     }
     __device__ __forceinline__ int bs1(int t, int b) const {
-        return (int)lds32(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+        return (int)lds32(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b, nb)));
     }
     // blocks b and its unit partner, stored adjacently (perm(b) even)
     __device__ __forceinline__ float2 dx2(int t, int b) const {
-        const uint2 v = lds64(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+        const uint2 v = lds64(dx + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b, nb)));
         return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
     }
     __device__ __forceinline__ int2 bs2(int t, int b) const {
-        const uint2 v = lds64(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b)));
+        const uint2 v = lds64(bs + 4u * (uint32_t)(t * nb + act_perm<TYPE>(b, nb)));
         return make_int2((int)v.x, (int)v.y);
     }
     // Q6_K unit: scales of blocks b and b + 2, adjacent after the permutation
@@ -265,8 +290,11 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
             acc[t] = fmaf(-(m2 * dd.y), i2f_exact(ss.y), acc[t]);
         }
     } else if constexpr (TYPE == kQ6_K) {
-        // unit = (super-block s, group g, pair pr): sub-blocks pr and pr+2 of group g
-        const int s = u >> 2, g = (u >> 1) & 1, pr = u & 1;
+        // unit u in the lane order of q6k_superblock_of (even super-blocks
+        // first) = (super-block s, group g, pair pr): sub-blocks pr and pr+2 of
+        // group g.  Every Q6_K path assigns units to lanes this way, so a row's
+        // result does not depend on M or on the path.
+        const int s = q6k_superblock_of(u, ((p.K >> 8) + 1) >> 1), g = (u >> 1) & 1, pr = u & 1;
         const uint32_t o = 210u * (uint32_t)s;
         uint32_t L[8], H[8], SC[2];
         src.template words<8, 2>(o + 64 * g + 32 * pr, L);
@@ -404,6 +432,198 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Specialised loops of the fused path for the two BASELINE weight types.
+// Same arithmetic as gemv_unit (identical integer partials, same per-block
+// FMA statements), with everything that is constant for a lane hoisted out
+// of the unit loop: the unit's position inside its super-block, the
+// swizzled activation offsets and the scale byte selectors.
+
+// byte `sel` of w as an exact float: 0x4B0000bb is 2^23 + bb.
+__device__ __forceinline__ float byte_as_float(uint32_t w, uint32_t sel) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | sel)) - 8388608.0f;
+}
+
+// byte `sel` of w sign-extended to int32: PRMT selector nibbles with bit 3
+// set replicate the sign of the selected byte.
+__device__ __forceinline__ int byte_as_int_signed(uint32_t w, uint32_t sel) {
+    int r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0u), "r"((sel | 8u) * 0x1110u | sel));
+    return r;
+}
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Q4_K row slice, activations and weights in shared memory (quant.cpp:549-590).
+// Lane unit u = 4s + q: sub-blocks 2q, 2q+1 of super-block s.
+template <int M>
+__device__ __forceinline__ void q4k_row_fused(uint32_t wrow, const ActSmem<kQ4_K>& act, int upr, int slice,
+                                              int wpr, float (&acc)[M]) {
+    const int lane = threadIdx.x & 31;
+    const int u0 = slice * 32 + lane;
+    const int ustep = 32 * wpr;
+    const int q = u0 & 3;
+    const bool low = q < 2;
+    const uint32_t sel0 = (uint32_t)(q & 1) * 2u, sel1 = sel0 + 1u;
+    const uint32_t key = (uint32_t)(u0 >> 1) & 7u;
+    // activation chunk u (64 bytes = blocks 2u, 2u+1), 16-byte pieces swizzled
+    const uint32_t cb = 16u * ((4u * (uint32_t)u0) ^ (key & 4u));
+    const uint32_t o0 = 16u * ((0u ^ key) & 3u), o1 = 16u * ((1u ^ key) & 3u);
+    const uint32_t o2 = 16u * ((2u ^ key) & 3u), o3 = 16u * ((3u ^ key) & 3u);
+    const uint32_t cstep = 64u * (uint32_t)ustep;
+    uint32_t wo = 144u * (uint32_t)(u0 >> 2);
+    const uint32_t wstep = 144u * (uint32_t)(ustep >> 2);
+    const uint32_t qoff = 16u + 32u * (uint32_t)q;
+    uint32_t ao = cb;                                // act byte offset of this lane's chunk
+    uint32_t so = 8u * (uint32_t)u0;                 // byte offset of (dx, bs) pair of block 2u
+    const uint32_t sstep = 8u * (uint32_t)ustep;
+#pragma unroll
+    for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+    for (int u = u0; u < upr; u += ustep, wo += wstep, ao += cstep, so += sstep) {
+        const uint4 h = lds128(wrow + wo);
+        const uint4 wa = lds128(wrow + wo + qoff), wb = lds128(wrow + wo + qoff + 16u);
+        const uint32_t scw = low ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+        const uint32_t mw = low ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+        const float d = h2f(h.x), dmin = h2f(h.x >> 16);
+        const float d1 = d * byte_as_float(scw, sel0), d2 = d * byte_as_float(scw, sel1);
+        const float m1 = dmin * byte_as_float(mw, sel0), m2 = dmin * byte_as_float(mw, sel1);
+        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        int lo[8];
+        uint32_t hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo[i] = (int)(w[i] & 0x0F0F0F0Fu);
+            hi[i] = w[i] & 0xF0F0F0F0u;  // 16 x high nibble, unsigned
+        }
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+            const uint32_t row = act.qx + (uint32_t)(t * act.kp) + ao;
+            const uint4 x0 = lds128(row + o0), x1 = lds128(row + o1), x2 = lds128(row + o2), x3 = lds128(row + o3);
+            int P0 = dp4a(lo[0], (int)x0.x, 0);
+            P0 = dp4a(lo[1], (int)x0.y, P0); P0 = dp4a(lo[2], (int)x0.z, P0); P0 = dp4a(lo[3], (int)x0.w, P0);
+            P0 = dp4a(lo[4], (int)x1.x, P0); P0 = dp4a(lo[5], (int)x1.y, P0);
+            P0 = dp4a(lo[6], (int)x1.z, P0); P0 = dp4a(lo[7], (int)x1.w, P0);
+            int H1 = dp4a_us(hi[0], (int)x2.x, 0);
+            H1 = dp4a_us(hi[1], (int)x2.y, H1); H1 = dp4a_us(hi[2], (int)x2.z, H1); H1 = dp4a_us(hi[3], (int)x2.w, H1);
+            H1 = dp4a_us(hi[4], (int)x3.x, H1); H1 = dp4a_us(hi[5], (int)x3.y, H1);
+            H1 = dp4a_us(hi[6], (int)x3.z, H1); H1 = dp4a_us(hi[7], (int)x3.w, H1);
+            const int P1 = H1 >> 4;  // exact: every term is a multiple of 16
+            const uint32_t sa = (uint32_t)(t * act.nb) * 4u + so;
+            const uint2 dd = lds64(act.dx + sa), ss = lds64(act.bs + sa);
+            const float dx0 = __uint_as_float(dd.x), dx1 = __uint_as_float(dd.y);
+            acc[t] = fmaf(d1 * dx0, i2f_exact(P0), acc[t]);
+            acc[t] = fmaf(-(m1 * dx0), i2f_exact((int)ss.x), acc[t]);
+            acc[t] = fmaf(d2 * dx1, i2f_exact(P1), acc[t]);
+            acc[t] = fmaf(-(m2 * dx1), i2f_exact((int)ss.y), acc[t]);
+        }
+    }
+    warp_sum<M>(acc);
+}
+
+
+// 8 words of a 32-byte field at shared address a, which is 4-byte aligned
+// (odd == false) or 2 bytes past a 4-byte boundary (odd == true).
+__device__ __forceinline__ void lds_field8(uint32_t a, bool odd, uint32_t (&w)[8]) {
+    if (!odd) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = lds32(a + 4u * i);
+    } else {
+        const uint32_t al = a - 2u;
+        uint32_t r[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) r[i] = lds32(al + 4u * i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = __funnelshift_r(r[i], r[i + 1], 16);
+    }
+}
+
+// Q6_K row slice, activations and weights in shared memory (quant.cpp:630-687).
+template <int M>
+__device__ __forceinline__ void q6k_row_fused(uint32_t wrow, const ActSmem<kQ6_K>& act, int upr, int slice,
+                                              int wpr, uint32_t quirk, float (&acc)[M]) {
+    const int lane = threadIdx.x & 31;
+    const int v0 = slice * 32 + lane;
+    const int vstep = 32 * wpr;
+    const int g = (v0 >> 1) & 1, pr = v0 & 1;
+    const int se = ((act.nb >> 3) + 1) >> 1;
+    const uint32_t key = (uint32_t)(v0 >> 1) & 7u;
+    const uint32_t o0 = 16u * ((0u ^ key) & 3u), o1 = 16u * ((1u ^ key) & 3u);
+    const uint32_t o2 = 16u * ((2u ^ key) & 3u), o3 = 16u * ((3u ^ key) & 3u);
+    const uint32_t loff = 64u * (uint32_t)g + 32u * (uint32_t)pr, hoff = 128u + 32u * (uint32_t)g;
+    const uint32_t scoff = 192u + 8u * (uint32_t)g;
+    const uint32_t sel0 = 2u * (uint32_t)pr, sel1 = sel0 + 1u;
+    const int hsh = 4 - 2 * pr, lsh = 2 * pr;
+#pragma unroll
+    for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+    for (int v = v0; v < upr; v += vstep) {
+        const int sb = q6k_superblock_of(v, se);
+        const uint32_t o = 210u * (uint32_t)sb;
+        const bool odd = (sb & 1) != 0;
+        uint32_t L[8], H[8];
+        lds_field8(wrow + o + loff, odd, L);
+        lds_field8(wrow + o + hoff, odd, H);
+        // 8 scale bytes of the group and d: 2-byte fields, 4-aligned when even
+        const uint32_t sa = wrow + o + scoff;
+        uint32_t SC0, SC1;
+        if (!odd) {
+            SC0 = lds32(sa);
+            SC1 = lds32(sa + 4u);
+        } else {
+            const uint32_t r0 = lds32(sa - 2u), r1 = lds32(sa + 2u), r2 = lds32(sa + 6u);
+            SC0 = __funnelshift_r(r0, r1, 16);
+            SC1 = __funnelshift_r(r1, r2, 16);
+        }
+        const float d = h2f(lds16(wrow + o + 208u));
+        const int sA0 = byte_as_int_signed(SC0, sel0), sA1 = byte_as_int_signed(SC0, sel1);
+        const int sB0 = byte_as_int_signed(SC1, sel0), sB1 = byte_as_int_signed(SC1, sel1);
+        // six-bit quants v in [0,63] per byte (the weight is v - 32)
+        uint32_t va[8], vb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            va[i] = (L[i] & 0x0F0F0F0Fu) | ((H[i] << hsh) & 0x30303030u);
+            vb[i] = ((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> lsh) & 0x30303030u);
+        }
+        const uint32_t cb = 16u * ((4u * (uint32_t)v) ^ (key & 4u));
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+            const uint32_t row = act.qx + (uint32_t)(t * act.kp) + cb;
+            const uint4 x0 = lds128(row + o0), x1 = lds128(row + o1), x2 = lds128(row + o2), x3 = lds128(row + o3);
+            const int xa[8] = {(int)x0.x, (int)x0.y, (int)x0.z, (int)x0.w, (int)x1.x, (int)x1.y, (int)x1.z, (int)x1.w};
+            const int xb[8] = {(int)x2.x, (int)x2.y, (int)x2.z, (int)x2.w, (int)x3.x, (int)x3.y, (int)x3.z, (int)x3.w};
+            // 32 x (half sums of q) of blocks 2v and 2v+1, then subtract: sum((v-32)*x)
+            const uint4 hsum = lds128(act.hs + 8u * (uint32_t)(t * act.nb + 2 * v));
+            int PA0 = -(int)hsum.x, PA1 = -(int)hsum.y, PB0 = -(int)hsum.z, PB1 = -(int)hsum.w;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                PA0 = dp4a((int)va[i], xa[i], PA0);
+                PA1 = dp4a((int)va[i + 4], xa[i + 4], PA1);
+                PB0 = dp4a((int)vb[i], xb[i], PB0);
+                PB1 = dp4a((int)vb[i + 4], xb[i + 4], PB1);
+            }
+            if ((quirk >> t) & 1u) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    PA0 += signtrick_fix(q6_to_s8(va[i]), xa[i]);
+                    PA1 += signtrick_fix(q6_to_s8(va[i + 4]), xa[i + 4]);
+                    PB0 += signtrick_fix(q6_to_s8(vb[i]), xb[i]);
+                    PB1 += signtrick_fix(q6_to_s8(vb[i + 4]), xb[i + 4]);
+                }
+            }
+            const uint2 dd = lds64(act.dx + 4u * (uint32_t)(t * act.nb + 2 * v));
+            // sc*P sums are exact integers (|.| <= 2^24), as the reference's float sums
+            const float inA = (float)(sA0 * PA0 + sA1 * PA1), inB = (float)(sB0 * PB0 + sB1 * PB1);
+            acc[t] = fmaf(d * __uint_as_float(dd.x), inA, acc[t]);
+            acc[t] = fmaf(d * __uint_as_float(dd.y), inB, acc[t]);
+        }
+    }
+    warp_sum<M>(acc);
+}
+
 // OR of the per-block -128 flags of each activation row (bit t = row t).
 // Only Q8_0 and Q6_K need it.  Must be called by all threads of the CTA.
 template <int TYPE, int M>
@@ -420,6 +640,27 @@ __device__ __forceinline__ uint32_t gemv_quirk_mask(const GemvParams& p) {
             if (__syncthreads_or(any)) mask |= 1u << t;
         }
         return mask;
+    }
+}
+
+// gemv_quirk_mask for the compute warps of the TMA kernel (producer excluded).
+template <int TYPE, int M>
+__device__ __forceinline__ uint32_t gemv_quirk_mask_compute(const GemvParams& p, uint32_t* s_quirk) {
+    if constexpr (TYPE != kQ8_0 && TYPE != kQ6_K) {
+        return 0u;
+    } else {
+        const int nb = p.K >> 5;
+        uint32_t mask = 0;
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+            int any = 0;
+            for (int i = threadIdx.x; i < nb; i += kGemvThreads) any |= p.fl[(int64_t)t * nb + i];
+            if (any) mask |= 1u << t;
+        }
+        const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
+        if ((threadIdx.x & 31) == 0 && wm) atomicOr(s_quirk, wm);
+        named_barrier_sync(kGemvThreads);
+        return *reinterpret_cast<volatile uint32_t*>(s_quirk);
     }
 }
 
@@ -482,10 +723,14 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
 // Returns the per-row "holds -128" mask.  Called by all threads.
 template <int M, int TYPE>
 __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
-                                                     uint8_t* qs, float* dx, int* bs) {
+                                                     uint8_t* qs, float* dx, int* bs, int* hs,
+                                                     uint32_t* s_quirk) {
     const int kp = act_row_stride(K);
-    constexpr int kGroups = kGemvThreads / 8;  // 32 blocks in flight per pass
-    constexpr int kUnroll = 4;
+    constexpr int kGroups = kGemvThreads / 8;  // 32 blocks per pass of the group loop
+    // Up to 16 blocks per group are loaded before any is reduced: one L2 round
+    // trip for M*K <= 16384 values (the activation loads queue behind the
+    // weight stream this CTA has already started, so round trips are slow).
+    constexpr int kUnroll = 8;
     const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
     const int nb = K >> 5;
     const int total = M * nb;
@@ -504,6 +749,8 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
+            // stop once no group of this warp has a block left (warp-uniform)
+            if (base + kGroups * u + (g & ~3) >= total) break;
             const int blk = base + g + kGroups * u;  // uniform within each 8-lane group
             const float a0 = fabsf(v[u].x), a1 = fabsf(v[u].y), a2 = fabsf(v[u].z), a3 = fabsf(v[u].w);
             // max over non-NaN values, as `if (a > amax) amax = a` from 0
@@ -519,83 +766,115 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
             const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float r = rintf(vv[e] * id);
-                int qi = (r >= -2147483648.0f && r < 2147483648.0f) ? (int)r : INT32_MIN;
+                // Round half to even without the conversion pipe: adding
+                // 1.5 * 2^23 leaves the rounded integer in the low mantissa
+                // bits for |v| < 2^22.  |v| <= 127 for every finite input;
+                // larger magnitudes only arise as +-inf or NaN (1/d overflowed
+                // or x was infinite), which x86 converts to INT32_MIN.
+                const float v = vv[e] * id;
+                const int qi = fabsf(v) < 4194304.0f ? __float_as_int(v + 12582912.0f) - 0x4B400000 : INT32_MIN;
                 q[e] = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
             }
-            int sum = q[0] + q[1] + q[2] + q[3];
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+            // lanes 0-3 of a group hold values 0-15 of the block, lanes 4-7 values 16-31
+            int half = q[0] + q[1] + q[2] + q[3];
+            half += __shfl_xor_sync(0xFFFFFFFFu, half, 1);
+            half += __shfl_xor_sync(0xFFFFFFFFu, half, 2);
+            const int sum = half + __shfl_xor_sync(0xFFFFFFFFu, half, 4);
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
                 const uint32_t packed = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) |
                                         ((uint32_t)(q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
-                const int pb = act_perm<TYPE>(b);
+                const int pb = act_perm<TYPE>(b, nb);
                 *reinterpret_cast<uint32_t*>(qs + t * kp + act_swizzle(32u * pb + 4u * sub)) = packed;
                 if ((q[0] == -128) | (q[1] == -128) | (q[2] == -128) | (q[3] == -128)) mask |= 1u << t;
                 if (sub == 0) {
                     dx[t * nb + pb] = d;
                     bs[t * nb + pb] = sum;
                 }
+                if (TYPE == kQ6_K && (sub & 3) == 0) hs[2 * (t * nb + pb) + (sub >> 2)] = 32 * half;
             }
         }
     }
-    uint32_t all = 0;
-#pragma unroll
-    for (int t = 0; t < M; ++t)
-        if (__syncthreads_or((int)((mask >> t) & 1u))) all |= 1u << t;
-    return all;
+    // OR over the compute warps (*s_quirk is zero on entry), then a barrier
+    // over those warps only: the producer warp does not take part.
+    const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
+    if ((threadIdx.x & 31) == 0 && wm) atomicOr(s_quirk, wm);
+    named_barrier_sync(kGemvThreads);
+    return *reinterpret_cast<volatile uint32_t*>(s_quirk);
 }
 
 // Shared-memory bytes the fused quantization needs for M rows of K.
 __host__ __device__ inline uint32_t fused_act_bytes(int M, int K) {
     const uint32_t nb = (uint32_t)K / 32u;
-    return (uint32_t)(M * act_row_stride(K)) + 8u * (uint32_t)M * nb;
+    return (uint32_t)(M * act_row_stride(K)) + 16u * (uint32_t)M * nb;
 }
 
+// Warp specialisation: warps 0..7 compute, warp 8 (one lane) streams the
+// weight tiles.  Stage s of the ring has a "full" barrier (one arrival plus
+// the bulk copy's transaction bytes) and an "empty" barrier (one arrival per
+// compute warp).  The producer refills a stage as soon as the eight compute
+// warps have released it, so warps do not run in lockstep: a warp that
+// finishes its row of tile i moves on to tile i+1 while others still work.
+// A row split over wpr > 1 warps is summed by the last of its warps to finish
+// (a shared counter per stage and row), in warp order, so the result does not
+// depend on timing.
 template <int TYPE, int M, bool EMIT, bool FUSED>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_tma_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    const int warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_addr(smem);
-    const uint32_t bar0 = sbase;                              // stages * 8 bytes
-    float* red = reinterpret_cast<float*>(smem + 128);        // 2 x kGemvWarps x M floats
-    int* s_abort = reinterpret_cast<int*>(smem + 64);
+    const uint32_t full0 = sbase + kHdrFull, empty0 = sbase + kHdrEmpty;
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kHdrAbort);
+    uint32_t* s_quirk = reinterpret_cast<uint32_t*>(smem + kHdrQuirk);
+    int* s_count = reinterpret_cast<int*>(smem + kHdrCount);
+    float* s_red = reinterpret_cast<float*>(smem + kHdrRed);
     const int nb = p.K >> 5;
     const uint32_t act_bytes = FUSED ? (fused_act_bytes(M, p.K) + 127u) / 128u * 128u : 0u;
     const uint32_t ring = sbase + kGemvSmemHeader + act_bytes;
     const int S = p.stages;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kGemvWarps);
+        }
         *s_abort = 0;
+        *s_quirk = 0;
         fence_mbar_init();
     }
+    for (int i = threadIdx.x; i < 64; i += blockDim.x) s_count[i] = 0;
     __syncthreads();
 
-    auto issue = [&](int tile, int stg) {
-        const int row0 = tile * p.rows_per_tile;
-        const int rows = min(p.rows_per_tile, p.N - row0);
-        const uint32_t bytes = (uint32_t)(rows * p.row_bytes);
-        mbar_arrive_expect_tx(bar0 + 8 * stg, bytes);
-        bulk_g2s(ring + stg * p.stage_bytes, p.w + (int64_t)row0 * p.row_bytes, bytes, bar0 + 8 * stg);
-    };
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            const int tile = blockIdx.x + s * gridDim.x;
-            if (tile < p.num_tiles) issue(tile, s);
+    // Programmatic dependent launch: the next kernel in the stream may start
+    // its own prologue (barrier set-up, weight prefetch) while this one runs.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == kGemvWarps) {
+        // ---- producer: weights are static, so no wait on the previous kernel
+        if (lane == 0) {
+            int it = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+                const int stg = it % S;
+                if (it >= S && !mbar_wait_or_abort(empty0 + 8 * stg, (uint32_t)((it / S) - 1) & 1u, s_abort))
+                    break;
+                const int row0 = tile * p.rows_per_tile;
+                const int rows = min(p.rows_per_tile, p.N - row0);
+                const uint32_t bytes = (uint32_t)(rows * p.row_bytes);
+                mbar_arrive_expect_tx(full0 + 8 * stg, bytes);
+                bulk_g2s(ring + stg * p.stage_bytes, p.w + (int64_t)row0 * p.row_bytes, bytes, full0 + 8 * stg);
+            }
+            // On abort, let every copy this CTA issued land before it exits.
+            if (*s_abort) {
+                const int issued = it;
+                for (int k = issued > S ? issued - S : 0; k < issued; ++k)
+                    mbar_wait_bounded(full0 + 8 * (k % S), (uint32_t)(k / S) & 1u);
+            }
         }
+        return;
     }
 
-    // Programmatic dependent launch: the next kernel in the stream may start
-    // its own prologue (barrier set-up, weight prefetch) while this one runs;
-    // the activations, which a previous kernel may produce, are read only
-    // after griddepcontrol.wait.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // ---- compute warps: activations are read after the previous kernel is done
     asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    // Activations: quantized here while the first weight tiles stream in, or
-    // read from the global workspace.
     uint32_t quirk;
     ActSmem<TYPE> as{};
     ActGmem ag{p.qx, p.dx, p.bs, p.K, nb};
@@ -604,45 +883,57 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_tma_kernel(const GemvPar
         const uint32_t qbytes = (uint32_t)(M * act_row_stride(p.K));
         float* dxs = reinterpret_cast<float*>(qs + qbytes);
         int* bss = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
-        const uint32_t qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss);
+        int* hss = reinterpret_cast<int*>(qs + qbytes + 8u * (uint32_t)(M * nb));
+        const uint32_t qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk);
         quirk = (TYPE == kQ8_0 || TYPE == kQ6_K) ? qm : 0u;
-        as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), act_row_stride(p.K), nb};
+        as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), smem_addr(hss), act_row_stride(p.K), nb};
     } else {
-        quirk = gemv_quirk_mask<TYPE, M>(p);
+        quirk = gemv_quirk_mask_compute<TYPE, M>(p, s_quirk);
     }
 
     const int r = warp / p.wpr, slice = warp - r * p.wpr;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         const int stg = it % S;
-        if (!mbar_wait_bounded(bar0 + 8 * stg, (uint32_t)(it / S) & 1u)) *s_abort = 1;
+        if (!mbar_wait_or_abort(full0 + 8 * stg, (uint32_t)(it / S) & 1u, s_abort)) break;
         const int row0 = tile * p.rows_per_tile;
         const int rows = min(p.rows_per_tile, p.N - row0);
-        float acc[M];
         if (r < rows) {
+            float acc[M];
             SmemSrc src{ring + stg * p.stage_bytes + (uint32_t)(r * p.row_bytes)};
-            if constexpr (FUSED) gemv_row_slice<TYPE, M, EMIT, 16>(src, as, row0 + r, p, slice, quirk, acc);
+            if constexpr (FUSED && TYPE == kQ4_K)
+                q4k_row_fused<M>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, acc);
+            else if constexpr (FUSED && TYPE == kQ6_K)
+                q6k_row_fused<M>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, quirk, acc);
+            else if constexpr (FUSED) gemv_row_slice<TYPE, M, EMIT, 16>(src, as, row0 + r, p, slice, quirk, acc);
             else gemv_row_slice<TYPE, M, EMIT, 16>(src, ag, row0 + r, p, slice, quirk, acc);
             if constexpr (!EMIT) {
-                if (p.wpr == 1) gemv_store_row<M>(row0 + r, acc, p);
-                else gemv_store_partial<M>(red + (it & 1) * kGemvWarps * M, warp, acc);
+                const int j = row0 + r;
+                if (p.wpr == 1) {
+                    gemv_store_row<M>(j, acc, p);
+                } else if (lane == 0) {
+                    float* red = s_red + (stg * kGemvWarps + warp) * 8;
+#pragma unroll
+                    for (int t = 0; t < M; ++t) red[t] = acc[t];
+                    __threadfence_block();
+                    int* cnt = s_count + stg * 8 + r;
+                    if (atomicAdd(cnt, 1) == p.wpr - 1) {
+                        __threadfence_block();
+                        *cnt = 0;
+                        const float b = p.bias ? p.bias[j] : 0.0f;
+#pragma unroll
+                        for (int t = 0; t < M; ++t) {
+                            float sum = 0.0f;
+                            for (int k = 0; k < p.wpr; ++k)
+                                sum += *reinterpret_cast<volatile float*>(s_red + (stg * kGemvWarps + r * p.wpr + k) * 8 + t);
+                            p.y[(int64_t)t * p.N + j] = sum + b;
+                        }
+                    }
+                }
             }
         }
-        __syncthreads();  // stage `stg` fully read; partial sums visible
-        if (*s_abort) break;
-        if (!EMIT && p.wpr > 1) gemv_combine<M>(red + (it & 1) * kGemvWarps * M, row0, rows, p);
-        if (threadIdx.x == 0) {
-            const int nt = tile + S * gridDim.x;
-            if (nt < p.num_tiles) issue(nt, stg);
-        }
-    }
-    if (*s_abort && threadIdx.x == 0) {
-        // Let every copy still in flight land before the CTA exits.
-        for (int k = 0; k < S; ++k) {
-            const int itk = it + k;
-            const int tile = blockIdx.x + itk * gridDim.x;
-            if (tile < p.num_tiles) mbar_wait_bounded(bar0 + 8 * (itk % S), (uint32_t)(itk / S) & 1u);
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * stg);
     }
 }
 

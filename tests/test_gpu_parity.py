@@ -103,17 +103,17 @@ def test_golden_fixtures(cuda, lib, t):
 def test_nan_activation_sign_trick(cuda, lib, oracle, t):
     """A NaN activation quantizes to -128; the reference's AVX2 Q8_0/Q6_K dots
     then form the sign-trick product, which the GPU reproduces exactly."""
-    k, n = 512, 64
-    w = synth.make_weights(t, n, k, seed=99)
-    x = synth.make_activations(2, k, 3)
-    x[0, [1, 2, 50, 300, 301]] = np.nan
-    _, qs, _ = oracle.quantize(x)
-    assert (qs == -128).sum() == 5
-    assert np.array_equal(G.partials(lib, qs, w, t, k, n), oracle.partials(w, t, k, n, qs))
-    y = G.matmul(lib, x, w, t, k, n)
-    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
-    assert np.all(np.isfinite(yo))
-    G.assert_rows_close(y, yo, ab, REL_TOL, "nan rows")
+    for k, n in ((512, 64), (4096, 96)):  # direct-load path and TMA path with fused quantization
+        w = synth.make_weights(t, n, k, seed=99)
+        x = synth.make_activations(2, k, 3)
+        x[0, [1, 2, 50, 300, 301]] = np.nan
+        _, qs, _ = oracle.quantize(x)
+        assert (qs == -128).sum() == 5
+        assert np.array_equal(G.partials(lib, qs, w, t, k, n), oracle.partials(w, t, k, n, qs))
+        y = G.matmul(lib, x, w, t, k, n)
+        yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+        assert np.all(np.isfinite(yo))
+        G.assert_rows_close(y, yo, ab, REL_TOL, f"nan rows k={k}")
 
 
 @pytest.mark.parametrize("t", HOT_TYPES, ids=IDS)
@@ -205,3 +205,18 @@ def test_baseline_layer_shapes(cuda, lib, oracle, name, t, k, n):
         y1 = G.matmul(lib, x[r:r + 1], w, t, k, n)
         assert np.array_equal(bits(y1[0]), bits(y4[r]))
     assert np.array_equal(bits(G.matmul(lib, x, w, t, k, n)), bits(y4))
+
+
+def test_plan_uses_tma_ring_and_fused_quantization(cuda, lib):
+    """The aligned BASELINE layer shapes run on the bulk-copy ring with the
+    activation quantization fused (one launch per call)."""
+    import ctypes
+
+    info = (ctypes.c_int * 8)()
+    w = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    for name, t, k, n in LAYER_SHAPES:
+        for m in (1, 4):
+            _lib.check(lib.cllm_cuda_matmul_plan(G.dptr(w), t, k, n, m, info, 8))
+            assert info[1] == 1, (name, m, list(info))
+            if not (m == 4 and k == 14336):
+                assert info[2] == 1 and info[0] == 1, (name, m, list(info))
