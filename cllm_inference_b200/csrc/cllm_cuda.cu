@@ -311,6 +311,37 @@ ActLayout act_layout(int m, int K, size_t at) {
     return L;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free entry point: a fixed scratch array for the quantized
+// activations of up to CLLM_NOALLOC_MAX_ROWS rows of CLLM_NOALLOC_MAX_IN_DIM
+// values, laid out as act_layout() lays out the workspace.
+constexpr size_t noalloc_scratch_bytes() {
+    return (size_t)CLLM_NOALLOC_MAX_ROWS * CLLM_NOALLOC_MAX_IN_DIM           // qs
+           + (size_t)CLLM_NOALLOC_MAX_ROWS * (CLLM_NOALLOC_MAX_IN_DIM / 32) * 9;  // dx, bsum, flags
+}
+static_assert(noalloc_scratch_bytes() == CLLM_NOALLOC_SCRATCH_BYTES, "scratch size in the header");
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CLLM_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  In host code the array's name is only a stand-in: passing it
+// to a kernel would not reach the device array.
+int noalloc_scratch(int dev, uint8_t** out) {
+    static std::mutex mu;
+    static uint8_t* addr[64] = {};
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(CLLM_ERR_CUDA, "matmul_quant_noalloc: cudaGetSymbolAddress failed: %s",
+                        cudaGetErrorString(e));
+        addr[dev] = static_cast<uint8_t*>(p);
+    }
+    *out = addr[dev];
+    return CLLM_OK;
+}
+
 }  // namespace
 }  // namespace cllm
 
@@ -621,6 +652,54 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
                          pl.stages, pl.grid, (int)pl.smem};
     for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];
     return CLLM_OK;
+}
+
+int cllm_cuda_matmul_quant_noalloc(const float* x, const void* w, int type, const float* bias,
+                                   int in_dim, int out_dim, int n_rows, float* y, void* stream) {
+    const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
+    if (n_rows <= 0) return CLLM_OK;
+    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
+    const int bsz = block_size_of(type);
+    if (in_dim % bsz != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
+    if (!has_vec_dot_of(type))
+        return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (n_rows > CLLM_NOALLOC_MAX_ROWS || in_dim > CLLM_NOALLOC_MAX_IN_DIM)
+        return fail(CLLM_ERR_TOO_LARGE,
+                    "matmul_quant_noalloc: at most %d rows of at most %d values (got %d x %d)",
+                    CLLM_NOALLOC_MAX_ROWS, CLLM_NOALLOC_MAX_IN_DIM, n_rows, in_dim);
+    if (out_dim == 0) return CLLM_OK;
+    if (!y || (in_dim > 0 && (!x || !w))) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    uint8_t* ws;
+    if (int rc = noalloc_scratch(dev, &ws)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row_bytes = (int64_t)(in_dim / bsz) * type_size_of(type);
+    const ActLayout L = act_layout(n_rows, in_dim, 0);
+    if (L.end > CLLM_NOALLOC_SCRATCH_BYTES)  // cannot happen within the limits above; kept as a guard
+        return fail(CLLM_ERR_TOO_LARGE, "matmul_quant_noalloc: %zu scratch bytes needed", L.end);
+    const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, n_rows,
+                                  false, di);
+    GemvParams p{};
+    p.w = static_cast<const uint8_t*>(w);
+    p.row_bytes = row_bytes;
+    p.K = in_dim;
+    p.N = out_dim;
+    p.x = x;
+    p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
+    p.dx = reinterpret_cast<float*>(ws + L.dx);
+    p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
+    p.fl = ws + L.fl;
+    p.bias = bias;
+    p.y = y;
+    p.partials = nullptr;
+    fill_plan(p, pl);
+    if (int rc = launch_quantize(x, in_dim, n_rows, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
+                                 const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
+        return rc;
+    return launch_gemv(type, false, n_rows, pl, p, st);
 }
 
 int cllm_cuda_check_device_status(void) {

@@ -133,6 +133,31 @@ int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void*
 int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int n_rows, int* info,
                           int n_info);
 
+/* Allocation-free matmul_quant, for callers that must not allocate device
+ * memory during the call: code being recorded into a CUDA graph (an
+ * allocation cannot be captured), engines whose own allocator already holds
+ * the device's memory, and latency-bound loops that cannot afford the device
+ * synchronisation that growing the regular entry point's workspace implies.
+ * No counterpart in the reference.
+ *
+ * Same arithmetic and results as cllm_cuda_matmul_quant with device pointers
+ * (x, w, bias, y all device memory; asynchronous on `stream`).  The quantized
+ * activations go to one fixed scratch array compiled into the library
+ * (CLLM_NOALLOC_SCRATCH_BYTES, held by every device that loads it until the
+ * process exits), so the call is limited to n_rows <= CLLM_NOALLOC_MAX_ROWS
+ * and in_dim <= CLLM_NOALLOC_MAX_IN_DIM; larger calls fail with
+ * CLLM_ERR_TOO_LARGE before any device work.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and caches it:
+ * make that first call before any stream capture.  All calls share the one
+ * array and every call rewrites the part it reads, so nothing needs clearing
+ * between calls, but calls that can overlap on the GPU (other streams,
+ * other host threads) race on it: serialise them. */
+#define CLLM_NOALLOC_MAX_ROWS 8
+#define CLLM_NOALLOC_MAX_IN_DIM 32768
+#define CLLM_NOALLOC_SCRATCH_BYTES 335872
+int cllm_cuda_matmul_quant_noalloc(const float* x, const void* w, int type, const float* bias,
+                                   int in_dim, int out_dim, int n_rows, float* y, void* stream);
+
 /* Read and clear the device-side status word that kernels set when a bounded
  * wait expires (CLLM_ERR_KERNEL_TIMEOUT); synchronizes the device. */
 int cllm_cuda_check_device_status(void);
