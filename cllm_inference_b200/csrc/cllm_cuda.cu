@@ -22,6 +22,7 @@
 #include "../../include/cllm_cuda.h"
 #include "common.cuh"
 #include "dequant.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "quantize.cuh"
 
@@ -296,6 +297,84 @@ int launch_quantize(const float* x, int64_t n, int rows, float* sc, int8_t* qs, 
     return CLLM_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Prefill (tcgen05) path
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn* out) {
+    static std::mutex mu;
+    static EncodeTiledFn fn = nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            return fail(CLLM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    *out = fn;
+    return CLLM_OK;
+}
+
+// 2-D tiled tensor map over a row-major [rows][cols] array.
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t cols,
+                uint64_t rows, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    EncodeTiledFn enc;
+    if (int rc = encode_fn(&enc)) return rc;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * (uint64_t)esize};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CLLM_OK;
+}
+
+bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_rows) {
+    return type == kQ4_K && n_rows >= kTcMinRows && K >= 256 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+           (row_bytes & 15) == 0;
+}
+
+// Workspace bytes of the prefill activations (fp16 q_x, dx, dx*bsum) for M rows of K.
+size_t prefill_bytes(int M, int K) {
+    const size_t nb = (size_t)K / 32;
+    return align256((size_t)M * K * 2) + align256((size_t)M * nb * 4) * 2;
+}
+
+// y[M][N] = batch matmul through prefill_q4k_kernel; x, w, bias, y on the device,
+// ws = prefill_bytes(M, K) of workspace.
+int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const float* bias, int K, int N, int M,
+                   float* y, uint8_t* ws, int dev, cudaStream_t st) {
+    const DeviceInfo& di = g_dev[dev];
+    const size_t nb = (size_t)K / 32;
+    const size_t off_a = 0, off_dx = align256((size_t)M * K * 2), off_xm = off_dx + align256((size_t)M * nb * 4);
+    __half* a16 = reinterpret_cast<__half*>(ws + off_a);
+    float* dxs = reinterpret_cast<float*>(ws + off_dx);
+    float* xmin = reinterpret_cast<float*>(ws + off_xm);
+    const int64_t blocks = (int64_t)M * (K / 32);
+    const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
+    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxs, xmin);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    CUtensorMap map_a, map_w;
+    if (int rc = make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, (uint64_t)K, (uint64_t)M, kTcBK, kTcBM,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    if (int rc = make_map_2d(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)row_bytes, (uint64_t)N, 144, kTcBN,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+    if (int rc = opt_in_smem(reinterpret_cast<const void*>(prefill_q4k_kernel), dev)) return rc;
+    TcParams tp{M, N, K, dxs, xmin, bias, y};
+    const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
+    prefill_q4k_kernel<<<tgrid, kTcThreads, kTcSmemBytes, st>>>(map_a, map_w, tp);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
 // Layout of the quantized activations inside the workspace.
 struct ActLayout {
     size_t qs, dx, bs, fl, end;
@@ -468,8 +547,9 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
             return fail(CLLM_ERR_INVALID_ARG, "%s: weight matrix runs past its registered range", fname);
     }
 
+    const bool use_tc = prefill_eligible(type, wd, row_bytes, in_dim, n_rows);
     const int mchunk = std::min(n_rows, 8);
-    const ActLayout L = act_layout(mchunk, in_dim, 0);
+    const ActLayout L = act_layout(use_tc ? 0 : mchunk, in_dim, 0);
     size_t off_x = L.end, off_b = L.end, off_y = L.end, total = L.end;
     if (flags & CLLM_X_HOST) {
         off_x = total;
@@ -481,6 +561,8 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
         off_y = total;
         total = align256(total + (size_t)n_rows * out_dim * 4);
     }
+    const size_t off_pre = total;
+    if (use_tc) total += prefill_bytes(n_rows, in_dim);
     uint8_t* ws;
     if (int rc = workspace(dev, total, &ws)) return rc;
 
@@ -497,7 +579,11 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
     }
     if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
 
-    for (int t0 = 0; t0 < n_rows; t0 += 8) {
+    if (use_tc) {
+        if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
+            return rc;
+    }
+    for (int t0 = 0; !use_tc && t0 < n_rows; t0 += 8) {
         const int m = std::min(8, n_rows - t0);
         const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di, xd + (size_t)t0 * in_dim);
         GemvParams p{};
@@ -648,8 +734,18 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
     const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, m, true,
                                   g_dev[dev]);
     const int chunks = n_rows <= 0 ? 0 : (n_rows + 7) / 8;
-    const int vals[8] = {chunks * (pl.fused ? 1 : 2), pl.tma, pl.fused, pl.rows_per_tile, pl.wpr,
-                         pl.stages, pl.grid, (int)pl.smem};
+    int vals[8] = {chunks * (pl.fused ? 1 : 2), pl.tma, pl.fused, pl.rows_per_tile, pl.wpr,
+                   pl.stages, pl.grid, (int)pl.smem};
+    if (prefill_eligible(type, w, row_bytes, in_dim, n_rows)) {
+        vals[0] = 2;  // activation preparation + the tcgen05 GEMM
+        vals[1] = 2;
+        vals[2] = 0;
+        vals[3] = kTcBN;
+        vals[4] = 0;
+        vals[5] = kTcStA;
+        vals[6] = ((n_rows + kTcBM - 1) / kTcBM) * ((out_dim + kTcBN - 1) / kTcBN);
+        vals[7] = (int)kTcSmemBytes;
+    }
     for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];
     return CLLM_OK;
 }

@@ -125,10 +125,11 @@ int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim
 int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream);
 
 /* Launch plan cllm_cuda_matmul_quant would use for these arguments (device
- * weights at w): info[0] kernels launched per call, [1] 1 if the weight tiles
- * stream through the bulk-copy (TMA) ring, [2] 1 if activation quantization
- * is fused into the dot kernel, [3] weight rows per tile, [4] warps per row,
- * [5] pipeline stages, [6] CTAs, [7] dynamic shared memory bytes.  No
+ * weights at w): info[0] kernels launched per call, [1] the dot kernel: 0
+ * direct loads, 1 bulk-copy (TMA) ring GEMV, 2 tcgen05 tensor-core GEMM
+ * (Q4_K batches of >= 64 rows), [2] 1 if activation quantization is fused
+ * into the dot kernel, [3] weight rows per tile, [4] warps per row, [5]
+ * pipeline stages, [6] CTAs, [7] dynamic shared memory bytes.  No
  * counterpart in the reference; used by tests and the benchmark. */
 int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int n_rows, int* info,
                           int n_info);

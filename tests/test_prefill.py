@@ -1,0 +1,50 @@
+"""Batched prefill (matmul_quant_batch, n_rows >= 64) on the tcgen05 GEMM
+against the oracle, with the same row tolerance as the decode path:
+|y_gpu - y_ref| <= 1e-5 * sum over the row's per-block float terms of |term|."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from cllm_inference_b200 import _lib, synth
+from tests import gpu_helpers as G
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-5
+
+# (K, N, M): a single tile, ragged token and row tiles, several super-blocks
+SHAPES = [(256, 128, 64), (256, 200, 100), (1024, 300, 129), (4096, 256, 128), (4096, 300, 257)]
+
+
+def plan(lib, w_ptr, t, k, n, m):
+    info = (ctypes.c_int * 8)()
+    _lib.check(lib.cllm_cuda_matmul_plan(w_ptr, t, k, n, m, info, 8))
+    return list(info)
+
+
+@pytest.mark.parametrize("k,n,m", SHAPES)
+def test_prefill_q4k_tcgen05(cuda, lib, oracle, k, n, m):
+    t = synth.Q4_K
+    w = synth.make_weights(t, n, k, seed=k + n + m)
+    x = synth.make_activations(m, k, seed=m)
+    bias = np.linspace(-2, 2, n, dtype=np.float32) if m % 2 else None
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2, "expected the tcgen05 path"
+    y = G.matmul(lib, x, w, t, k, n, bias=bias)
+    yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+    G.assert_rows_close(y, yo, ab, REL_TOL, f"prefill {k}x{n} m={m}")
+
+
+def test_prefill_matches_decode_rows(cuda, lib):
+    """Rows of a 64-row prefill equal 1-row calls within the row tolerance."""
+    from oracle.oracle import Oracle
+
+    t, k, n, m = synth.Q4_K, 4096, 160, 64
+    w = synth.make_weights(t, n, k, seed=3)
+    x = synth.make_activations(m, k, seed=4)
+    y = G.matmul(lib, x, w, t, k, n)
+    _, ab = Oracle().matmul(x[:8], w, t, k, n, with_abs=True)
+    for r in range(8):
+        y1 = G.matmul(lib, x[r:r + 1], w, t, k, n)
+        G.assert_rows_close(y[r:r + 1], y1, ab[r:r + 1], 2 * REL_TOL, f"row {r}")
