@@ -343,7 +343,7 @@ bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_r
 // Workspace bytes of the prefill activations (fp16 q_x, dx, dx*bsum) for M rows of K.
 size_t prefill_bytes(int M, int K) {
     const size_t nb = (size_t)K / 32;
-    return align256((size_t)M * K * 2) + align256((size_t)M * nb * 4) * 2;
+    return align256((size_t)M * K * 2) + align256((size_t)M * nb * 8);
 }
 
 // y[M][N] = batch matmul through prefill_q4k_kernel; x, w, bias, y on the device,
@@ -352,15 +352,17 @@ int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const fl
                    float* y, uint8_t* ws, int dev, cudaStream_t st) {
     const DeviceInfo& di = g_dev[dev];
     const size_t nb = (size_t)K / 32;
-    const size_t off_a = 0, off_dx = align256((size_t)M * K * 2), off_xm = off_dx + align256((size_t)M * nb * 4);
+    const size_t off_a = 0, off_dx = align256((size_t)M * K * 2);
     __half* a16 = reinterpret_cast<__half*>(ws + off_a);
-    float* dxs = reinterpret_cast<float*>(ws + off_dx);
-    float* xmin = reinterpret_cast<float*>(ws + off_xm);
+    float* dxx = reinterpret_cast<float*>(ws + off_dx);  // [M][2*nb]: (dx, dx*bsum)
     const int64_t blocks = (int64_t)M * (K / 32);
     const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
-    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxs, xmin);
+    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx);
     CLLM_CUDA_TRY(cudaGetLastError());
-    CUtensorMap map_a, map_w;
+    CUtensorMap map_a, map_w, map_dx;
+    if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxx, (uint64_t)(2 * nb), (uint64_t)M, 16, kTcBM,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
     if (int rc = make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, (uint64_t)K, (uint64_t)M, kTcBK, kTcBM,
                              CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
@@ -368,9 +370,9 @@ int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const fl
                              CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
     if (int rc = opt_in_smem(reinterpret_cast<const void*>(prefill_q4k_kernel), dev)) return rc;
-    TcParams tp{M, N, K, dxs, xmin, bias, y};
+    TcParams tp{M, N, K, bias, y};
     const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
-    prefill_q4k_kernel<<<tgrid, kTcThreads, kTcSmemBytes, st>>>(map_a, map_w, tp);
+    prefill_q4k_kernel<<<tgrid, kTcThreads, kTcSmemBytes, st>>>(map_a, map_w, map_dx, tp);
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }

@@ -7,12 +7,14 @@
 // multiplies exact small integers on the tensor core with kind::f16:
 //   A = activations as fp16 q_x (|q_x| <= 128, exact),
 //   B = Q4_K weights dequantized in shared memory to fp16 sc*q (<= 945, exact),
-// one TMEM accumulator region per 32-value block.  Every product and every
-// partial sum is an integer below 2^22, so each block's accumulator is the
-// exact sc*P_b.  The epilogue then applies one FMA per element and block with
-// dx, which is constant along a TMEM lane (a token), and once per 256-value
-// super-block y += d * acc - dmin * sum_b m_b * (dx_b * bsum_b).
-//
+// one TMEM accumulator per 32-value block.  Every product and every partial
+// sum is an integer below 2^22, so each block's accumulator is the exact
+// sc*P_b.  With r_b = dmin*m_b/d per weight row and sub-block, the epilogue
+// keeps acc = sum_b dx_b * (sc*P_b - bsum_b * r_b) in registers (two FMAs per
+// element and block; dx is constant along a TMEM lane, i.e. a token) and once
+// per 256-value super-block adds y += d * acc into a TMEM-resident y.  A
+// super-block with d == 0 is dequantized with sc = 0 and scaled by 1, so its
+// contribution is the min term alone.
 // Tile: 128 tokens (MMA M, TMEM lanes) x 128 weight rows (MMA N), K in
 // chunks of 64 (one 128-byte SW128 row of fp16).  Warp roles (14 warps):
 //   0      producer: TMA tiles of the fp16 activations and of the raw Q4_K
@@ -35,13 +37,15 @@ constexpr int kTcWarps = 14;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr uint32_t kTcTileBytes = kTcBM * kTcBK * 2;  // 16 KB fp16 operand tile
 constexpr uint32_t kTcRawBytes = kTcBN * 144;         // one Q4_K super-block per row
-constexpr uint32_t kTcScBytes = kTcBN * 9 * 4;        // d and dmin*m[8] per row
+constexpr uint32_t kTcScBytes = kTcBN * 9 * 4;        // d[128], then r[8][128]
+constexpr uint32_t kTcDxBytes = kTcBM * 16 * 4;       // (dx, dx*bsum) of 8 blocks per token
 // shared-memory layout (offsets from a 1024-aligned base)
 constexpr uint32_t kTcOffA = 0;
 constexpr uint32_t kTcOffB = kTcOffA + kTcStA * kTcTileBytes;
 constexpr uint32_t kTcOffRaw = kTcOffB + kTcStB * kTcTileBytes;
 constexpr uint32_t kTcOffSc = kTcOffRaw + kTcStRaw * kTcRawBytes;
-constexpr uint32_t kTcOffBar = kTcOffSc + 2 * kTcScBytes;
+constexpr uint32_t kTcOffDx = kTcOffSc + 2 * kTcScBytes;
+constexpr uint32_t kTcOffBar = kTcOffDx + 2 * kTcDxBytes;
 constexpr uint32_t kTcSmemBytes = kTcOffBar + 512 + 1024;  // + alignment slack
 // barrier indices (8 bytes each, from kTcOffBar)
 enum : int {
@@ -49,7 +53,8 @@ enum : int {
     kBarBEmpty = kBarBFull + kTcStB, kBarRawFull = kBarBEmpty + kTcStB,
     kBarRawEmpty = kBarRawFull + kTcStRaw, kBarScFull = kBarRawEmpty + kTcStRaw,
     kBarScEmpty = kBarScFull + 2, kBarDFull = kBarScEmpty + 2, kBarDEmpty = kBarDFull + kTcDBuf,
-    kBarMmaDone = kBarDEmpty + kTcDBuf, kBarCount = kBarMmaDone + 1
+    kBarDxFull = kBarDEmpty + kTcDBuf, kBarDxEmpty = kBarDxFull + 2,
+    kBarMmaDone = kBarDxEmpty + 2, kBarCount = kBarMmaDone + 1
 };
 constexpr uint32_t kTcOffTmem = kTcOffBar + 8 * kBarCount;  // u32 TMEM base address
 constexpr uint32_t kTcOffAbort = kTcOffTmem + 4;
@@ -57,8 +62,6 @@ static_assert(kTcOffAbort + 4 <= kTcOffBar + 512, "barrier area");
 
 struct TcParams {
     int M, N, K;
-    const float* dx;    // [M][K/32] activation block scales
-    const float* xmin;  // [M][K/32] dx * bsum (the Q4_K min term's activation side)
     const float* bias;  // [N] or nullptr
     float* y;           // [M][N]
 };
@@ -133,6 +136,50 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Wait on an mbarrier phase as a whole warp: lane 0 polls, the outcome is
+// broadcast, so warp-collective tcgen05 instructions that follow see every
+// lane on the same path.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+    int ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_or_abort(bar, parity, abort) ? 1 : 0;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+__device__ __forceinline__ void sts128(uint32_t a, float x, float y, float z, float w) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+
 // fp16 pair (sc*n0, sc*n1) from two 4-bit values in bytes b0, b1 of w: the
 // pair 0x64nn is 1024 + n exactly, and fma(1024 + n, sc, -1024 sc) = sc*n is
 // exact (it is an integer <= 945, rounded once).
@@ -160,9 +207,11 @@ __device__ __forceinline__ uint32_t half2_bits(float v) {
     return b | (b << 16);
 }
 
+// 14 warps put 4 warps on some SM sub-partitions (16384 registers each), so
+// 128 registers per thread is the ceiling.
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_q4k_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                       const TcParams p) {
+                       const __grid_constant__ CUtensorMap map_dx, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_addr(smem);
@@ -170,7 +219,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int tok0 = blockIdx.x * kTcBM, row0 = blockIdx.y * kTcBN;
     const int nsb = p.K >> 8;         // super-blocks
     const int nchunk = p.K / kTcBK;   // 64-value chunks
-    const int nblk = p.K >> 5;        // 32-value blocks
     auto bar = [&](int i) { return sb + kTcOffBar + 8u * (uint32_t)i; };
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kTcOffAbort);
     volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(smem + kTcOffTmem);
@@ -181,6 +229,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < kTcStRaw; ++i) { mbar_init(bar(kBarRawFull + i), 1); mbar_init(bar(kBarRawEmpty + i), 4); }
         for (int i = 0; i < 2; ++i) { mbar_init(bar(kBarScFull + i), 4); mbar_init(bar(kBarScEmpty + i), 8); }
         for (int i = 0; i < kTcDBuf; ++i) { mbar_init(bar(kBarDFull + i), 1); mbar_init(bar(kBarDEmpty + i), 8); }
+        for (int i = 0; i < 2; ++i) { mbar_init(bar(kBarDxFull + i), 1); mbar_init(bar(kBarDxEmpty + i), 8); }
         mbar_init(bar(kBarMmaDone), 1);
         *s_abort = 0;
         fence_mbar_init();
@@ -207,6 +256,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_arrive_expect_tx(bar(kBarRawFull + rs), kTcRawBytes);
                 tma_load_2d(sb + kTcOffRaw + rs * kTcRawBytes, &map_w, 144 * s, row0, bar(kBarRawFull + rs));
                 ++issued_raw;
+                const int xs = s & 1;
+                if (s >= 2 && !mbar_wait_or_abort(bar(kBarDxEmpty + xs), (uint32_t)((s >> 1) - 1) & 1u, s_abort))
+                    break;
+                mbar_arrive_expect_tx(bar(kBarDxFull + xs), kTcDxBytes);
+                tma_load_2d(sb + kTcOffDx + xs * kTcDxBytes, &map_dx, 16 * s, tok0, bar(kBarDxFull + xs));
                 for (int q = 0; q < 4; ++q) {
                     const int c = 4 * s + q, as = c % kTcStA;
                     if (c >= kTcStA &&
@@ -259,32 +313,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp < 6) {
         // ---------------- dequantization: thread i owns weight row i of the tile
         const int i = threadIdx.x - 64;
-        float* scs = reinterpret_cast<float*>(smem + kTcOffSc);
         for (int s = 0; s < nsb; ++s) {
             const int rs = s % kTcStRaw;
             if (!mbar_wait_or_abort(bar(kBarRawFull + rs), (uint32_t)(s / kTcStRaw) & 1u, s_abort)) break;
             const uint32_t rb = sb + kTcOffRaw + rs * kTcRawBytes + 144u * (uint32_t)i;
             const uint4 hd = lds128(rb);
-            uint32_t q[32];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint4 v = lds128(rb + 16u + 16u * k);
-                q[4 * k] = v.x; q[4 * k + 1] = v.y; q[4 * k + 2] = v.z; q[4 * k + 3] = v.w;
-            }
             // 6-bit scales and mins of the 8 sub-blocks (get_scale_min_k4, quant.cpp:72-80)
-            const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
-            const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
-            const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
             const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
-            // epilogue scales for this super-block: d, and dmin*m per sub-block
+            // d == 0 zeroes the main term: B gets sc = 0 and the epilogue scale becomes 1
+            const bool dz = (d == 0.0f);
+            const float d_eff = dz ? 1.0f : d;
+            const uint32_t sc_lo = dz ? 0u : (hd.y & 0x3F3F3F3Fu), m_lo = hd.z & 0x3F3F3F3Fu;
+            const uint32_t sc_hi = dz ? 0u : ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u));
+            const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+            // epilogue scales for this super-block: d, and r_k = dmin*m_k/d per sub-block, so that
+            // d * sum_k dx_k (P_k - bsum_k r_k) = sum_k (d dx_k P_k - dmin m_k dx_k bsum_k)
             const int ss = s & 1;
             if (s >= 2 && !mbar_wait_or_abort(bar(kBarScEmpty + ss), (uint32_t)((s >> 1) - 1) & 1u, s_abort)) break;
-            float* sco = scs + ss * (kTcBN * 9) + i * 9;
-            sco[0] = d;
+            const uint32_t sco = sb + kTcOffSc + (uint32_t)ss * kTcScBytes;
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(sco + 4u * (uint32_t)i), "f"(d_eff) : "memory");
+            // r as [8][128]: one sub-block's values for consecutive rows are contiguous
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const uint32_t mw = k < 4 ? m_lo : m_hi;
-                sco[1 + k] = dmin * (float)((mw >> (8 * (k & 3))) & 0xFFu);
+                const float r = (dmin * (float)((mw >> (8 * (k & 3))) & 0xFFu)) / d_eff;
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(sco + 4u * (uint32_t)(kTcBN * (k + 1) + i)), "f"(r)
+                             : "memory");
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarScFull + ss));
@@ -302,9 +356,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // row i of B (128 bytes = 64 fp16): values 0..31 = sub-block 2pq (low nibbles of
                 // q[32pq..32pq+31]), values 32..63 = sub-block 2pq+1 (high nibbles)
                 const uint32_t brow = sb + kTcOffB + bs * kTcTileBytes + (uint32_t)(i >> 3) * 1024u + (uint32_t)(i & 7) * 128u;
+                // the 32 quant bytes of sub-block pair pq
+                const uint4 qa = lds128(rb + 16u + 32u * (uint32_t)pq), qb = lds128(rb + 32u + 32u * (uint32_t)pq);
+                const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
                 for (int ch = 0; ch < 8; ++ch) {
-                    const int w0i = 8 * pq + 2 * (ch & 3);
+                    const int w0i = 2 * (ch & 3);
                     uint32_t w0 = q[w0i], w1 = q[w0i + 1];
                     uint4 o;
                     if (ch < 4) {
@@ -328,83 +385,95 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
         // ---------------- epilogue: thread = token, 64 columns
         const int quad = warp & 3, half = (warp - 6) >> 2;
-        const int t = tok0 + 32 * quad + lane;
-        const bool tok_ok = t < p.M;
+        const int tl = 32 * quad + lane;  // token within the tile = TMEM lane
+        const int t = tok0 + tl;
         const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
         const uint32_t ycol = (uint32_t)(kTcDBuf * kTcBN + 64 * half);  // running y in TMEM
-        const float* scs = reinterpret_cast<const float*>(smem + kTcOffSc);
-        const float* dxrow = p.dx + (int64_t)(tok_ok ? t : 0) * nblk;
-        const float* xmrow = p.xmin + (int64_t)(tok_ok ? t : 0) * nblk;
         float acc[64];
         for (int s = 0; s < nsb; ++s) {
+            const int xs = s & 1, ss = s & 1;
+            if (!warp_wait(bar(kBarDxFull + xs), (uint32_t)(s >> 1) & 1u, s_abort)) break;
+            if (!warp_wait(bar(kBarScFull + ss), (uint32_t)(s >> 1) & 1u, s_abort)) break;
+            // (dx, dx*bsum) of blocks 8s..8s+7 for this token
+            const uint32_t dxa = sb + kTcOffDx + (uint32_t)xs * kTcDxBytes + 64u * (uint32_t)tl;
+            const uint32_t sca = sb + kTcOffSc + (uint32_t)ss * kTcScBytes;
 #pragma unroll
             for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
             bool ok = true;
 #pragma unroll 1
             for (int k = 0; k < 8; ++k) {
                 const int b = 8 * s + k, db = b % kTcDBuf;
-                const float dxk = tok_ok ? __ldg(dxrow + b) : 0.0f;  // issued before the wait
-                if (!mbar_wait_or_abort(bar(kBarDFull + db), (uint32_t)(b / kTcDBuf) & 1u, s_abort)) {
+                if (!warp_wait(bar(kBarDFull + db), (uint32_t)(b / kTcDBuf) & 1u, s_abort)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                float dv[32];
                 const uint32_t dcol = tmem + lane_base + (uint32_t)(db * kTcBN + 64 * half);
-                tmem_ld32(dcol, dv);
+                const uint32_t rq = sca + 4u * (uint32_t)(kTcBN * (k + 1) + 64 * half);
+                float dxk, xmk;
+                asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(dxk), "=f"(xmk) : "r"(dxa + 8u * (uint32_t)k));
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[j] = fmaf(dxk, dv[j], acc[j]);
-                tmem_ld32(dcol + 32u, dv);
+                for (int g = 0; g < 4; ++g) {
+                    float dv[16];
+                    tmem_ld16(dcol + 16u * g, dv);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(dxk, dv[j], acc[32 + j]);
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 r = lds128f(rq + 64u * g + 16u * j4);
+                        const float rv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = 16 * g + 4 * j4 + e;
+                            acc[j] = fmaf(dxk, dv[4 * j4 + e], acc[j]);
+                            acc[j] = fmaf(-xmk, rv[e], acc[j]);
+                        }
+                    }
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarDEmpty + db));
             }
             if (!ok) break;
-            // super-block end: y += d * acc - sum_k (dmin m_k) * (dx_k bsum_k)
-            const int ss = s & 1;
-            if (!mbar_wait_or_abort(bar(kBarScFull + ss), (uint32_t)(s >> 1) & 1u, s_abort)) break;
-            const float* sc = scs + ss * (kTcBN * 9) + (64 * half) * 9;
+            // super-block end: y += d * acc
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                float yv[32];
-                const uint32_t ya = tmem + lane_base + ycol + 32u * hh;
+            for (int cg = 0; cg < 4; ++cg) {
+                float yv[16];
+                const uint32_t ya = tmem + lane_base + ycol + 16u * cg;
                 if (s > 0) {
-                    tmem_ld32(ya, yv);
+                    tmem_ld16(ya, yv);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) yv[j] = 0.0f;
+                    for (int j = 0; j < 16; ++j) yv[j] = 0.0f;
                 }
-                float xm[8];
+                const uint32_t dq = sca + 4u * (uint32_t)(64 * half + 16 * cg);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) xm[kk] = tok_ok ? __ldg(xmrow + 8 * s + kk) : 0.0f;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float* cs = sc + (32 * hh + j) * 9;
-                    float mn = 0.0f;
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) mn = fmaf(cs[1 + kk], xm[kk], mn);
-                    yv[j] = fmaf(cs[0], acc[32 * hh + j], yv[j]) - mn;
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 d = lds128f(dq + 16u * j4);
+                    yv[4 * j4 + 0] = fmaf(d.x, acc[16 * cg + 4 * j4 + 0], yv[4 * j4 + 0]);
+                    yv[4 * j4 + 1] = fmaf(d.y, acc[16 * cg + 4 * j4 + 1], yv[4 * j4 + 1]);
+                    yv[4 * j4 + 2] = fmaf(d.z, acc[16 * cg + 4 * j4 + 2], yv[4 * j4 + 2]);
+                    yv[4 * j4 + 3] = fmaf(d.w, acc[16 * cg + 4 * j4 + 3], yv[4 * j4 + 3]);
                 }
-                tmem_st32(ya, yv);
+                tmem_st16(ya, yv);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarScEmpty + ss));
+            if (lane == 0) {
+                mbar_arrive(bar(kBarScEmpty + ss));
+                mbar_arrive(bar(kBarDxEmpty + xs));
+            }
         }
-        // write y (+ bias)
-        if (!*s_abort) {
+        // write y (+ bias); tcgen05.ld is warp-collective, so every lane loads
+        const int aborted = __shfl_sync(0xFFFFFFFFu, *s_abort, 0);
+        if (!aborted) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                float yv[32];
-                tmem_ld32(tmem + lane_base + ycol + 32u * hh, yv);
-                const int j0 = row0 + 64 * half + 32 * hh;
-                if (tok_ok) {
+            for (int cg = 0; cg < 4; ++cg) {
+                float yv[16];
+                tmem_ld16(tmem + lane_base + ycol + 16u * cg, yv);
+                const int j0 = row0 + 64 * half + 16 * cg;
+                if (t < p.M) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < 16; ++j)
                         if (j0 + j < p.N) p.y[(int64_t)t * p.N + j0 + j] = yv[j] + (p.bias ? p.bias[j0 + j] : 0.0f);
-                    }
                 }
             }
         }
@@ -419,10 +488,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // Prefill activation preparation: quantize_row_q8_0 per 32-value block
-// (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16, dx, and dx*bsum.
+// (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16 and the pairs
+// (dx, dx*bsum) per block.
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ x, int64_t n,
                                                            int64_t total_blocks, __half* __restrict__ a16,
-                                                           float* __restrict__ dx, float* __restrict__ xmin) {
+                                                           float* __restrict__ dxx) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int64_t nb = n >> 5;
@@ -443,9 +513,9 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
         int s = q;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if (lane == 0) {
-            dx[r * nb + b] = d;
-            xmin[r * nb + b] = d * (float)s;
+        if (lane == 0) {  // (dx, dx*bsum) pairs, [M][2*nb]
+            dxx[2 * (r * nb + b)] = d;
+            dxx[2 * (r * nb + b) + 1] = d * (float)s;
         }
     }
 }
