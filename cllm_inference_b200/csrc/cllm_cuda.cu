@@ -369,10 +369,19 @@ int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const fl
     if (int rc = make_map_2d(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)row_bytes, (uint64_t)N, 144, kTcBN,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
+    // y leaves through TMA stores when its rows are 16-byte multiples; else plain stores
+    CUtensorMap map_y;
+    std::memset(&map_y, 0, sizeof(map_y));
+    const int tma_store = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) ? 1 : 0;
+    if (tma_store) {
+        if (int rc = make_map_2d(&map_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, (uint64_t)N, (uint64_t)M, 32, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    }
     if (int rc = opt_in_smem(reinterpret_cast<const void*>(prefill_q4k_kernel), dev)) return rc;
-    TcParams tp{M, N, K, bias, y};
+    TcParams tp{M, N, K, bias, y, tma_store};
     const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
-    prefill_q4k_kernel<<<tgrid, kTcThreads, kTcSmemBytes, st>>>(map_a, map_w, map_dx, tp);
+    prefill_q4k_kernel<<<tgrid, kTcThreads, kTcSmemBytes, st>>>(map_a, map_w, map_dx, map_y, tp);
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }

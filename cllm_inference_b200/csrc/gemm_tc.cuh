@@ -64,6 +64,7 @@ struct TcParams {
     int M, N, K;
     const float* bias;  // [N] or nullptr
     float* y;           // [M][N]
+    int tma_store;      // 1: y through map_y (N % 4 == 0, y 16-byte aligned)
 };
 
 // ---- PTX wrappers --------------------------------------------------------
@@ -74,6 +75,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "[%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -160,6 +168,23 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.ld without the wait, and the wait tied to the destination registers
+// (as in/out operands) so that no use of them can move above it.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
 // Wait on an mbarrier phase as a whole warp: lane 0 polls, the outcome is
 // broadcast, so warp-collective tcgen05 instructions that follow see every
 // lane on the same path.
@@ -207,11 +232,34 @@ __device__ __forceinline__ uint32_t half2_bits(float v) {
     return b | (b << 16);
 }
 
+// One 16-column group G of a block in the epilogue: per element
+// acc = fma(dx, D, acc), then acc = fma(-dx*bsum, r, acc).  (Packed f32x2 FMAs
+// here raise register pressure past the 128-register ceiling.)
+template <int G>
+__device__ __forceinline__ void epi_group(float2 (&acc)[32], const uint32_t (&v)[16], uint32_t rq, float2 dx2,
+                                          float2 nx2) {
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+        const float4 r = lds128f(rq + 64u * G + 16u * j4);
+        float2& a0 = acc[8 * G + 2 * j4];
+        float2& a1 = acc[8 * G + 2 * j4 + 1];
+        a0.x = fmaf(dx2.x, __uint_as_float(v[4 * j4]), a0.x);
+        a0.y = fmaf(dx2.x, __uint_as_float(v[4 * j4 + 1]), a0.y);
+        a1.x = fmaf(dx2.x, __uint_as_float(v[4 * j4 + 2]), a1.x);
+        a1.y = fmaf(dx2.x, __uint_as_float(v[4 * j4 + 3]), a1.y);
+        a0.x = fmaf(nx2.x, r.x, a0.x);
+        a0.y = fmaf(nx2.x, r.y, a0.y);
+        a1.x = fmaf(nx2.x, r.z, a1.x);
+        a1.y = fmaf(nx2.x, r.w, a1.y);
+    }
+}
+
 // 14 warps put 4 warps on some SM sub-partitions (16384 registers each), so
 // 128 registers per thread is the ceiling.
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_q4k_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                       const __grid_constant__ CUtensorMap map_dx, const TcParams p) {
+                       const __grid_constant__ CUtensorMap map_dx, const __grid_constant__ CUtensorMap map_y,
+                       const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_addr(smem);
@@ -389,7 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int t = tok0 + tl;
         const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
         const uint32_t ycol = (uint32_t)(kTcDBuf * kTcBN + 64 * half);  // running y in TMEM
-        float acc[64];
+        float2 acc[32];
         for (int s = 0; s < nsb; ++s) {
             const int xs = s & 1, ss = s & 1;
             if (!warp_wait(bar(kBarDxFull + xs), (uint32_t)(s >> 1) & 1u, s_abort)) break;
@@ -398,7 +446,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t dxa = sb + kTcOffDx + (uint32_t)xs * kTcDxBytes + 64u * (uint32_t)tl;
             const uint32_t sca = sb + kTcOffSc + (uint32_t)ss * kTcScBytes;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
             bool ok = true;
 #pragma unroll 1
             for (int k = 0; k < 8; ++k) {
@@ -412,25 +460,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t rq = sca + 4u * (uint32_t)(kTcBN * (k + 1) + 64 * half);
                 float dxk, xmk;
                 asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(dxk), "=f"(xmk) : "r"(dxa + 8u * (uint32_t)k));
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    float dv[16];
-                    tmem_ld16(dcol + 16u * g, dv);
-#pragma unroll
-                    for (int j4 = 0; j4 < 4; ++j4) {
-                        const float4 r = lds128f(rq + 64u * g + 16u * j4);
-                        const float rv[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int j = 16 * g + 4 * j4 + e;
-                            acc[j] = fmaf(dxk, dv[4 * j4 + e], acc[j]);
-                            acc[j] = fmaf(-xmk, rv[e], acc[j]);
-                        }
-                    }
-                }
+                const float2 dx2 = make_float2(dxk, dxk), nx2 = make_float2(-xmk, -xmk);
+                // the TMEM load of the next 16 columns overlaps the FMAs of the current ones
+                uint32_t v0[16], v1[16];
+                tmem_ld16_issue(dcol, v0);
+                tmem_ld_wait(v0);
+                tmem_ld16_issue(dcol + 16u, v1);
+                epi_group<0>(acc, v0, rq, dx2, nx2);
+                tmem_ld_wait(v1);
+                tmem_ld16_issue(dcol + 32u, v0);
+                epi_group<1>(acc, v1, rq, dx2, nx2);
+                tmem_ld_wait(v0);
+                tmem_ld16_issue(dcol + 48u, v1);
+                epi_group<2>(acc, v0, rq, dx2, nx2);
+                tmem_ld_wait(v1);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarDEmpty + db));
+                epi_group<3>(acc, v1, rq, dx2, nx2);
             }
             if (!ok) break;
             // super-block end: y += d * acc
@@ -448,10 +495,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int j4 = 0; j4 < 4; ++j4) {
                     const float4 d = lds128f(dq + 16u * j4);
-                    yv[4 * j4 + 0] = fmaf(d.x, acc[16 * cg + 4 * j4 + 0], yv[4 * j4 + 0]);
-                    yv[4 * j4 + 1] = fmaf(d.y, acc[16 * cg + 4 * j4 + 1], yv[4 * j4 + 1]);
-                    yv[4 * j4 + 2] = fmaf(d.z, acc[16 * cg + 4 * j4 + 2], yv[4 * j4 + 2]);
-                    yv[4 * j4 + 3] = fmaf(d.w, acc[16 * cg + 4 * j4 + 3], yv[4 * j4 + 3]);
+                    const float2 y0 = __ffma2_rn(make_float2(d.x, d.y), acc[8 * cg + 2 * j4],
+                                                 make_float2(yv[4 * j4], yv[4 * j4 + 1]));
+                    const float2 y1 = __ffma2_rn(make_float2(d.z, d.w), acc[8 * cg + 2 * j4 + 1],
+                                                 make_float2(yv[4 * j4 + 2], yv[4 * j4 + 3]));
+                    yv[4 * j4] = y0.x; yv[4 * j4 + 1] = y0.y; yv[4 * j4 + 2] = y1.x; yv[4 * j4 + 3] = y1.y;
                 }
                 tmem_st16(ya, yv);
             }
@@ -464,7 +512,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         // write y (+ bias); tcgen05.ld is warp-collective, so every lane loads
         const int aborted = __shfl_sync(0xFFFFFFFFu, *s_abort, 0);
-        if (!aborted) {
+        if (!aborted && p.tma_store) {
+            // Stage this warp's 32 tokens x 64 columns in the (now idle) A-operand
+            // buffers as two 32x32 fp32 boxes in the 128-byte swizzled layout, then
+            // one TMA store per box; TMA clips rows >= M and columns >= N.
+            const uint32_t stage = sb + kTcOffA + (uint32_t)(warp - 6) * 8192u;
+#pragma unroll
+            for (int cg = 0; cg < 4; ++cg) {
+                float yv[16];
+                tmem_ld16(tmem + lane_base + ycol + 16u * cg, yv);
+                const int j0 = row0 + 64 * half + 16 * cg;
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) yv[j] += (j0 + j < p.N) ? p.bias[j0 + j] : 0.0f;
+                }
+                const uint32_t box = stage + (uint32_t)(cg >> 1) * 4096u + (uint32_t)lane * 128u;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t chunk = (uint32_t)((cg & 1) * 4 + q) ^ (uint32_t)(lane & 7);
+                    sts128(box + (chunk << 4), yv[4 * q], yv[4 * q + 1], yv[4 * q + 2], yv[4 * q + 3]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+#pragma unroll
+                for (int bx = 0; bx < 2; ++bx)
+                    tma_store_2d(&map_y, row0 + 64 * half + 32 * bx, tok0 + 32 * quad, stage + 4096u * bx);
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+            }
+            __syncwarp();
+        } else if (!aborted) {
 #pragma unroll
             for (int cg = 0; cg < 4; ++cg) {
                 float yv[16];
