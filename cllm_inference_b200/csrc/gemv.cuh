@@ -716,82 +716,87 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
 }
 
 // Quantize x [M][K] into this CTA's shared memory (quantize_row_q8_0,
-// quant.cpp:420-452, the same IEEE steps as quantize_q8_0_kernel).  Eight
-// lanes share a 32-value block, one float4 each; every thread issues the
-// loads of four blocks before reducing them, so the prologue costs about one
-// L2 round trip per four blocks per group.  x must be 16-byte aligned.
-// Returns the per-row "holds -128" mask.  Called by all threads.
+// quant.cpp:420-452, the same IEEE steps as quantize_q8_0_kernel).  Four
+// lanes share a 32-value block, eight values (two float4) each, so the two
+// divisions per block and the packing are spread over eight values per lane;
+// every thread issues the loads of up to four blocks before reducing them.
+// x must be 16-byte aligned.  Returns the per-row "holds -128" mask.  Called
+// by all compute threads.
 template <int M, int TYPE>
 __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
                                                      uint8_t* qs, float* dx, int* bs, int* hs,
                                                      uint32_t* s_quirk) {
     const int kp = act_row_stride(K);
-    constexpr int kGroups = kGemvThreads / 8;  // 32 blocks per pass of the group loop
-    // Up to 16 blocks per group are loaded before any is reduced: one L2 round
-    // trip for M*K <= 16384 values (the activation loads queue behind the
-    // weight stream this CTA has already started, so round trips are slow).
-    constexpr int kUnroll = 8;
-    const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
+    constexpr int kGroups = kGemvThreads / 4;  // 64 blocks per pass of the group loop
+    constexpr int kUnroll = 4;
+    const int g = threadIdx.x >> 2, sub = threadIdx.x & 3;
     const int nb = K >> 5;
     const int total = M * nb;
+    const uint32_t a_qs = smem_addr(qs);
     uint32_t mask = 0;
     for (int base = 0; base < total; base += kGroups * kUnroll) {
-        float4 v[kUnroll];
+        float4 v[kUnroll][2];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int blk = base + g + kGroups * u;
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
-                v[u] = __ldg(reinterpret_cast<const float4*>(x + (int64_t)t * K + 32 * b + 4 * sub));
+                const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t * K + 32 * b + 8 * sub);
+                v[u][0] = __ldg(src);
+                v[u][1] = __ldg(src + 1);
             } else {
-                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u][0] = v[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             // stop once no group of this warp has a block left (warp-uniform)
-            if (base + kGroups * u + (g & ~3) >= total) break;
-            const int blk = base + g + kGroups * u;  // uniform within each 8-lane group
-            const float a0 = fabsf(v[u].x), a1 = fabsf(v[u].y), a2 = fabsf(v[u].z), a3 = fabsf(v[u].w);
-            // max over non-NaN values, as `if (a > amax) amax = a` from 0
-            float amax = (a0 > 0.0f) ? a0 : 0.0f;
-            amax = (a1 > amax) ? a1 : amax;
-            amax = (a2 > amax) ? a2 : amax;
-            amax = (a3 > amax) ? a3 : amax;
+            if (base + kGroups * u + (g & ~7) >= total) break;
+            const int blk = base + g + kGroups * u;  // uniform within each 4-lane group
+            const float vv[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                                 v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+            // max of |x| over non-NaN values, as `if (a > amax) amax = a` from 0
+            float amax = 0.0f;
 #pragma unroll
-            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(vv[e]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
             const float d = amax / 127.0f;
-            const float id = (d != 0.0f) ? 1.0f / d : 0.0f;
-            int q[4];
-            const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+            const float id = (d != 0.0f) ? __frcp_rn(d) : 0.0f;  // == 1.0f / d, correctly rounded
+            int q[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
+            for (int e = 0; e < 8; ++e) {
                 // Round half to even without the conversion pipe: adding
                 // 1.5 * 2^23 leaves the rounded integer in the low mantissa
                 // bits for |v| < 2^22.  |v| <= 127 for every finite input;
                 // larger magnitudes only arise as +-inf or NaN (1/d overflowed
                 // or x was infinite), which x86 converts to INT32_MIN.
-                const float v = vv[e] * id;
-                const int qi = fabsf(v) < 4194304.0f ? __float_as_int(v + 12582912.0f) - 0x4B400000 : INT32_MIN;
+                const float f = vv[e] * id;
+                const int qi = fabsf(f) < 4194304.0f ? __float_as_int(f + 12582912.0f) - 0x4B400000 : INT32_MIN;
                 q[e] = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
             }
-            // lanes 0-3 of a group hold values 0-15 of the block, lanes 4-7 values 16-31
-            int half = q[0] + q[1] + q[2] + q[3];
-            half += __shfl_xor_sync(0xFFFFFFFFu, half, 1);
-            half += __shfl_xor_sync(0xFFFFFFFFu, half, 2);
-            const int sum = half + __shfl_xor_sync(0xFFFFFFFFu, half, 4);
+            const uint32_t w0 = __byte_perm(__byte_perm((uint32_t)q[0], (uint32_t)q[1], 0x0040u),
+                                            __byte_perm((uint32_t)q[2], (uint32_t)q[3], 0x0040u), 0x5410u);
+            const uint32_t w1 = __byte_perm(__byte_perm((uint32_t)q[4], (uint32_t)q[5], 0x0040u),
+                                            __byte_perm((uint32_t)q[6], (uint32_t)q[7], 0x0040u), 0x5410u);
+            // sums: 8 values per lane, 16 per lane pair (half block), 32 per group
+            const int s8 = __dp4a((int)w0, 0x01010101, __dp4a((int)w1, 0x01010101, 0));
+            const int half = s8 + __shfl_xor_sync(0xFFFFFFFFu, s8, 1);
+            const int sum = half + __shfl_xor_sync(0xFFFFFFFFu, half, 2);
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
-                const uint32_t packed = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) |
-                                        ((uint32_t)(q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
                 const int pb = act_perm<TYPE>(b, nb);
-                *reinterpret_cast<uint32_t*>(qs + t * kp + act_swizzle(32u * pb + 4u * sub)) = packed;
-                if ((q[0] == -128) | (q[1] == -128) | (q[2] == -128) | (q[3] == -128)) mask |= 1u << t;
+                const uint32_t a = a_qs + (uint32_t)(t * kp) + act_swizzle(32u * pb + 8u * sub);
+                asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(w0), "r"(w1) : "memory");
+                // a byte equal to 0x80 (-128): zero byte of w ^ 0x80808080
+                const uint32_t z0 = w0 ^ 0x80808080u, z1 = w1 ^ 0x80808080u;
+                if (((z0 - 0x01010101u) & ~z0 & 0x80808080u) | ((z1 - 0x01010101u) & ~z1 & 0x80808080u))
+                    mask |= 1u << t;
                 if (sub == 0) {
                     dx[t * nb + pb] = d;
                     bs[t * nb + pb] = sum;
                 }
-                if (TYPE == kQ6_K && (sub & 3) == 0) hs[2 * (t * nb + pb) + (sub >> 2)] = 32 * half;
+                if (TYPE == kQ6_K && (sub & 1) == 0) hs[2 * (t * nb + pb) + (sub >> 1)] = 32 * half;
             }
         }
     }
