@@ -50,6 +50,9 @@ SIGNATURES = {
     "cllm_cuda_dequantize": (_I, [_P, _I, _I64, _P, _P]),
     "cllm_cuda_matmul_plan": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_I), _I]),
     "cllm_cuda_matmul_quant_noalloc": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _P]),
+    "cllm_cuda_shard_rows": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
+    "cllm_cuda_matmul_quant_rowshard": (_I, [_P, _P, _I, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_P), _P]),
+    "cllm_cuda_shard_barrier": (_I, [ctypes.POINTER(_P), _P, _I, _I, _P]),
     "cllm_cuda_check_device_status": (_I, []),
     "cllm_cuda_last_error": (_I, [ctypes.c_char_p, _SZ]),
 }

@@ -24,6 +24,7 @@
 #include "dequant.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "shard.cuh"
 #include "quantize.cuh"
 
 namespace cllm {
@@ -248,7 +249,9 @@ int opt_in_smem(const void* fn, int dev) {
     return CLLM_OK;
 }
 
-int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams& p, cudaStream_t st) {
+int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams& p_in, cudaStream_t st) {
+    GemvParams p = p_in;
+    if (p.ldy == 0) p.ldy = p.N;
     GemvFn fn = select_gemv(type, pl.tma, pl.fused, emit, m);
     if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no kernel for type %d, %d rows", type, m);
     if (pl.smem > 48 * 1024) {
@@ -807,6 +810,94 @@ int cllm_cuda_matmul_quant_noalloc(const float* x, const void* w, int type, cons
                                  const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
         return rc;
     return launch_gemv(type, false, n_rows, pl, p, st);
+}
+
+int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* rows) {
+    if (out_dim < 0 || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !row_begin || !rows)
+        return fail(CLLM_ERR_INVALID_ARG, "shard_rows: bad arguments (out_dim %d, world %d, rank %d)", out_dim,
+                    world, rank);
+    shard_rows(out_dim, world, rank, row_begin, rows);
+    return CLLM_OK;
+}
+
+int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int type, const float* bias,
+                                    int in_dim, int out_dim, int rank, int world, int n_rows,
+                                    float* const* y_peers, void* stream) {
+    const char* fname = "matmul_quant_rowshard";
+    if (n_rows <= 0) return CLLM_OK;
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !y_peers)
+        return fail(CLLM_ERR_INVALID_ARG, "%s: bad group (world %d, rank %d)", fname, world, rank);
+    if (n_rows > 8) return fail(CLLM_ERR_TOO_LARGE, "%s: at most 8 activation rows (got %d)", fname, n_rows);
+    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
+    const int bsz = block_size_of(type);
+    if (in_dim % bsz != 0) return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    int row0, rows;
+    shard_rows(out_dim, world, rank, &row0, &rows);
+    for (int q = 0; q < world; ++q)
+        if (!y_peers[q]) return fail(CLLM_ERR_INVALID_ARG, "%s: null y buffer of rank %d", fname, q);
+    if (rows == 0) return CLLM_OK;
+    if (in_dim > 0 && (!x || !w_shard)) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row_bytes = (int64_t)(in_dim / bsz) * type_size_of(type);
+    const uint8_t* wd = static_cast<const uint8_t*>(w_shard);
+    const ActLayout L = act_layout(n_rows, in_dim, 0);
+    // The tile shape of the UNSHARDED call (it fixes how a row's units are split
+    // over lanes and warps, hence the float order of the row sum), so every
+    // output equals the one-GPU result bit for bit; only the tile count shrinks.
+    GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, n_rows, true, di, x);
+    pl.num_tiles = (rows + pl.rows_per_tile - 1) / pl.rows_per_tile;
+    pl.grid = std::max(1, std::min(pl.grid, pl.num_tiles));
+    uint8_t* ws = nullptr;
+    if (!pl.fused) {
+        if (int rc = workspace(dev, L.end, &ws)) return rc;
+    }
+    GemvParams p{};
+    p.w = wd;
+    p.row_bytes = row_bytes;
+    p.K = in_dim;
+    p.N = rows;
+    p.x = x;
+    if (ws) {
+        p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
+        p.dx = reinterpret_cast<float*>(ws + L.dx);
+        p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
+        p.fl = ws + L.fl;
+    }
+    p.bias = bias ? bias + row0 : nullptr;
+    p.y = y_peers[rank] + row0;
+    p.partials = nullptr;
+    fill_plan(p, pl);
+    p.ldy = out_dim;
+    p.npeers = world;
+    for (int q = 0; q < world; ++q) p.ypeers[q] = y_peers[q] + row0;
+    if (!pl.fused) {
+        if (int rc = launch_quantize(x, in_dim, n_rows, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
+                                     const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
+            return rc;
+    }
+    return launch_gemv(type, false, n_rows, pl, p, st);
+}
+
+int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream) {
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !signal_pads || !epoch)
+        return fail(CLLM_ERR_INVALID_ARG, "shard_barrier: bad arguments (world %d, rank %d)", world, rank);
+    ShardSignal sg{};
+    for (int q = 0; q < world; ++q) {
+        if (!signal_pads[q]) return fail(CLLM_ERR_INVALID_ARG, "shard_barrier: null signal pad of rank %d", q);
+        sg.pads[q] = signal_pads[q];
+    }
+    sg.epoch = epoch;
+    sg.world = world;
+    sg.rank = rank;
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    shard_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(sg);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
 }
 
 int cllm_cuda_check_device_status(void) {

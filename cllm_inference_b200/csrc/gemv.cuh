@@ -22,6 +22,8 @@
 
 namespace cllm {
 
+constexpr int kMaxPeers = 8;  // GPUs of one node that a row-sharded call writes to
+
 struct GemvParams {
     const uint8_t* w;     // weight matrix, out_dim rows of row_bytes
     int64_t row_bytes;
@@ -40,6 +42,9 @@ struct GemvParams {
     int num_tiles;
     int stages;
     uint32_t stage_bytes;
+    int64_t ldy;          // row stride of y (0: N); set per launch
+    int npeers;           // > 0: row-sharded call, y goes to every ypeers[q] instead of y
+    float* ypeers[kMaxPeers];
 };
 
 constexpr int kGemvWarps = 8;                      // warps that compute (R rows x wpr warps per row)
@@ -692,6 +697,18 @@ __device__ __forceinline__ void gemv_store_partial(float* red, int warp, const f
 }
 
 // y = sum of the wpr warp partials of each row (in warp order) + bias.
+// Store y[t][j]: locally, or (row-sharded call) into the y buffer of every GPU
+// of the group over NVLink peer mappings, so the output is all-gathered as it
+// is produced.
+__device__ __forceinline__ void gemv_put(const GemvParams& p, int t, int j, float v) {
+    const int64_t o = (int64_t)t * p.ldy + j;
+    if (p.npeers == 0) {
+        p.y[o] = v;
+        return;
+    }
+    for (int q = 0; q < p.npeers; ++q) p.ypeers[q][o] = v;
+}
+
 template <int M>
 __device__ __forceinline__ void gemv_combine(const float* red, int row0, int rows,
                                              const GemvParams& p) {
@@ -702,7 +719,7 @@ __device__ __forceinline__ void gemv_combine(const float* red, int row0, int row
         for (int k = 0; k < p.wpr; ++k) s += red[(r * p.wpr + k) * M + t];
         const int j = row0 + r;
         if (p.bias) s += p.bias[j];
-        p.y[(int64_t)t * p.N + j] = s;
+        gemv_put(p, t, j, s);
     }
 }
 
@@ -711,7 +728,7 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
     if ((threadIdx.x & 31) == 0) {
         const float b = p.bias ? p.bias[j] : 0.0f;
 #pragma unroll
-        for (int t = 0; t < M; ++t) p.y[(int64_t)t * p.N + j] = acc[t] + b;
+        for (int t = 0; t < M; ++t) gemv_put(p, t, j, acc[t] + b);
     }
 }
 
@@ -931,7 +948,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
                             float sum = 0.0f;
                             for (int k = 0; k < p.wpr; ++k)
                                 sum += *reinterpret_cast<volatile float*>(s_red + (stg * kGemvWarps + r * p.wpr + k) * 8 + t);
-                            p.y[(int64_t)t * p.N + j] = sum + b;
+                            gemv_put(p, t, j, sum + b);
                         }
                     }
                 }
@@ -940,6 +957,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * stg);
     }
+    // row-sharded call: this thread's peer stores are visible system-wide before
+    // the kernel ends (the barrier kernel that follows announces them)
+    if (p.npeers > 0) __threadfence_system();
 }
 
 template <int TYPE, int M, bool EMIT>
@@ -967,6 +987,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_direct_kernel(const GemvPar
             __syncthreads();
         }
     }
+    if (p.npeers > 0) __threadfence_system();
 }
 
 }  // namespace cllm

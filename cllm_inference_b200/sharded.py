@@ -1,0 +1,164 @@
+"""Row-sharded matmul_quant across the GPUs of one node (one process per GPU).
+
+The 70B decode configuration splits every weight matrix by output rows over
+`world` GPUs: rank r keeps rows [begin_r, begin_r + rows_r) in HBM in native
+block layout and computes that slice of y = W x.  Row sharding never splits a
+quantization block, and every row is summed exactly as on one GPU, so the
+gathered y equals the unsharded matmul_quant result bit for bit.
+
+Two ways to gather the slices:
+
+* ``RowShardGroup.matmul`` -- the product path.  The GEMV stores each output
+  element straight into the y buffer of every rank (NVLink peer mappings of
+  symmetric memory), then one small barrier kernel exchanges a release/acquire
+  signal per pair of GPUs (``cllm_cuda_matmul_quant_rowshard`` +
+  ``cllm_cuda_shard_barrier``).  No separate collective runs.
+* ``RowShardGroup.matmul_nccl`` -- the baseline: the local GEMV, then
+  ``all_gather_into_tensor`` over NCCL and a reorder (``gather_rows``).
+
+The reference has no multi-GPU code; the single-GPU call it replaces is
+``matmul_quant`` (src/core/quant.cpp:1374-1431).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import _lib, synth
+
+
+def shard_rows(out_dim: int, world: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) of `rank`'s slice (cllm_cuda_shard_rows)."""
+    lib = _lib.load()
+    b, r = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(lib.cllm_cuda_shard_rows(out_dim, world, rank, ctypes.byref(b), ctypes.byref(r)))
+    return b.value, r.value
+
+
+def shard_weight_bytes(w, type_: int, in_dim: int, out_dim: int, world: int, rank: int):
+    """This rank's rows of a [out_dim] x row_bytes weight matrix (any 1-D uint8 tensor
+    or array), as a view: rows are contiguous in the GGML row-major layout."""
+    rb = synth.row_bytes(type_, in_dim)
+    begin, rows = shard_rows(out_dim, world, rank)
+    return w[begin * rb:(begin + rows) * rb]
+
+
+def gather_rows(local, out_dim: int, group=None):
+    """All-gather row slices: local is this rank's [n_rows, rows_r] output; returns
+    the full [n_rows, out_dim] on every rank.  Slices are padded to the largest
+    one for all_gather_into_tensor and put back in row order."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n_rows = local.shape[0]
+    spans = [shard_rows(out_dim, world, q) for q in range(world)]
+    width = max(r for _, r in spans)
+    assert local.shape[1] == spans[rank][1]
+    padded = torch.zeros(n_rows, width, dtype=local.dtype, device=local.device)
+    padded[:, :local.shape[1]] = local
+    gathered = torch.empty(world * n_rows, width, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(gathered, padded, group=group)
+    gathered = gathered.view(world, n_rows, width)
+    out = torch.empty(n_rows, out_dim, dtype=local.dtype, device=local.device)
+    for q, (b, r) in enumerate(spans):
+        out[:, b:b + r] = gathered[q, :, :r]
+    return out
+
+
+class ShardedWeight:
+    """One rank's rows of a quantized weight matrix, resident in HBM."""
+
+    def __init__(self, data, type_: int, in_dim: int, out_dim: int, world: int, rank: int):
+        self.data = data  # uint8 CUDA tensor, rows x row_bytes
+        self.type = type_
+        self.in_dim = in_dim
+        self.out_dim = out_dim
+        self.begin, self.rows = shard_rows(out_dim, world, rank)
+
+
+class RowShardGroup:
+    """The GPUs of a torch.distributed group (backend nccl, one process per GPU)
+    running row-sharded matmul_quant calls.
+
+    max_out / max_rows size the two symmetric y buffers (double-buffered: a
+    fast rank may write call n+1's slice while a slow rank still reads call
+    n's result)."""
+
+    def __init__(self, max_out: int, max_rows: int = 8, group=None):
+        import torch
+        import torch.distributed as dist
+
+        # plain peer loads and stores only: no NVLink multicast objects
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > 8:
+            raise ValueError("row sharding is limited to the 8 GPUs of one node")
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.lib = _lib.load()
+        _lib.check(self.lib.cllm_cuda_init(self.dev.index))
+        self.max_out, self.max_rows = max_out, max_rows
+        gname = self.group.group_name
+        self._y = [symm.empty(max_rows * max_out, dtype=torch.float32, device=self.dev) for _ in range(2)]
+        self._sig = symm.empty(64, dtype=torch.int32, device=self.dev)
+        self._sig.zero_()
+        self._epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        torch.cuda.synchronize()
+        hy = [symm.rendezvous(t, gname) for t in self._y]
+        hs = symm.rendezvous(self._sig, gname)
+        arr = ctypes.c_void_p * self.world
+        self._yptrs = [arr(*[int(p) for p in h.buffer_ptrs]) for h in hy]
+        self._sigptrs = arr(*[int(p) for p in hs.buffer_ptrs])
+        self._handles = hy + [hs]
+        self._flip = 0
+        dist.barrier(group=self.group)
+
+    def shard(self, w_full, type_: int, in_dim: int, out_dim: int) -> ShardedWeight:
+        """Copy this rank's rows of a full weight matrix (uint8 tensor, host or
+        device) into HBM."""
+        part = shard_weight_bytes(w_full, type_, in_dim, out_dim, self.world, self.rank)
+        return ShardedWeight(part.to(self.dev).contiguous(), type_, in_dim, out_dim, self.world, self.rank)
+
+    def matmul(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None, out=None):
+        """y = W x for the full W (every rank gets all out_dim outputs).  x:
+        [n_rows, in_dim] fp32 on this GPU, the same on every rank; bias: full
+        out_dim fp32 or None.  Returns [n_rows, out_dim] (a copy, or `out`)."""
+        import torch
+
+        if n_rows > self.max_rows or sw.out_dim > self.max_out:
+            raise ValueError("call larger than the group's y buffers")
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        buf = self._flip
+        self._flip ^= 1
+        _lib.check(self.lib.cllm_cuda_matmul_quant_rowshard(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
+            ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, sw.in_dim, sw.out_dim,
+            self.rank, self.world, n_rows, self._yptrs[buf], st))
+        _lib.check(self.lib.cllm_cuda_shard_barrier(self._sigptrs, ctypes.c_void_p(self._epoch.data_ptr()),
+                                                    self.world, self.rank, st))
+        y = self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
+        if out is None:
+            return y.clone()
+        out.copy_(y)
+        return out
+
+    def matmul_nccl(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
+        """The same result through the local GEMV and an NCCL all-gather."""
+        import torch
+
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        local = torch.empty(n_rows, sw.rows, dtype=torch.float32, device=self.dev)
+        b = bias[sw.begin:sw.begin + sw.rows].contiguous() if bias is not None else None
+        _lib.check(self.lib.cllm_cuda_matmul_quant(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
+            ctypes.c_void_p(b.data_ptr()) if b is not None else None, sw.in_dim, sw.rows, n_rows,
+            ctypes.c_void_p(local.data_ptr()), 0, st))
+        return gather_rows(local, sw.out_dim, self.group)
+
+    def close(self):
+        self._handles = []

@@ -159,6 +159,44 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
 int cllm_cuda_matmul_quant_noalloc(const float* x, const void* w, int type, const float* bias,
                                    int in_dim, int out_dim, int n_rows, float* y, void* stream);
 
+/* ---- Row-sharded decode across the GPUs of one node ----
+ * Replaces matmul_quant (quant.cpp:1374-1431) for a weight matrix split by
+ * output rows over `world` GPUs (one process per GPU): rank r holds rows
+ * [row_begin, row_begin + rows) of every matrix, as cllm_cuda_shard_rows
+ * assigns them.  Row sharding never splits a block, and each row's sum is
+ * computed exactly as on one GPU, so the gathered y is identical to the
+ * unsharded call's. */
+
+/* The rows of an out_dim-row matrix owned by `rank` of `world` (<= 8): as
+ * even as possible, the first out_dim % world ranks one row more.  Host only. */
+int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* rows);
+
+/* y[t][j] for this rank's rows j, written into the y buffer of EVERY rank:
+ * y_peers[q] (q < world) is rank q's [n_rows][out_dim] fp32 buffer as mapped
+ * into this process (NVLink peer mapping, e.g. symmetric memory), so the
+ * output is all-gathered by the GEMV's own stores.  x: [n_rows][in_dim] fp32
+ * on this device (the full activation, the same on every rank); w_shard:
+ * this rank's rows only (rows x row_bytes, native blocks, device memory);
+ * bias: the full out_dim bias or NULL.  n_rows <= 8.  Asynchronous: y is
+ * complete on a rank only after cllm_cuda_shard_barrier. */
+int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int type, const float* bias,
+                                    int in_dim, int out_dim, int rank, int world, int n_rows,
+                                    float* const* y_peers, void* stream);
+
+/* Completion barrier of a row-sharded call: tells every rank that this
+ * rank's slice has landed (a release store of the new epoch into slot `rank`
+ * of signal_pads[q], q < world) and waits until every rank has reached the
+ * same epoch (slot q of signal_pads[rank]).  signal_pads: each rank's
+ * zero-initialised array of >= world uint32 words, peer-mapped; epoch: this
+ * rank's own zero-initialised device word, advanced by one per barrier on the
+ * GPU (so a CUDA graph that replays the barrier stays in step).  Every rank
+ * must run the same sequence of barriers.  The wait is bounded (1 s): a
+ * missing rank ends it with the device status set
+ * (cllm_cuda_check_device_status then reports CLLM_ERR_KERNEL_TIMEOUT).
+ * Double-buffer y across consecutive calls: a rank may start writing call
+ * n+1's slice while a slower rank still reads call n's y. */
+int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream);
+
 /* Read and clear the device-side status word that kernels set when a bounded
  * wait expires (CLLM_ERR_KERNEL_TIMEOUT); synchronizes the device. */
 int cllm_cuda_check_device_status(void);
