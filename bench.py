@@ -51,6 +51,13 @@ LAYER = [("q", synth.Q4_K, 4096, 4096), ("k", synth.Q4_K, 4096, 1024), ("v", syn
          ("down", synth.Q6_K, 14336, 4096)]
 LM_HEAD = ("lm_head", synth.Q6_K, 4096, 128256)
 FALLBACK_HBM_GBS = 6650.0
+# Llama-3-70B shapes, every matrix row-sharded over the GPUs
+LAYER_70B = [("q", synth.Q4_K, 8192, 8192), ("k", synth.Q4_K, 8192, 1024), ("v", synth.Q4_K, 8192, 1024),
+             ("o", synth.Q4_K, 8192, 8192), ("gate", synth.Q4_K, 8192, 28672), ("up", synth.Q4_K, 8192, 28672),
+             ("down", synth.Q6_K, 28672, 8192)]
+LM_HEAD_70B = ("lm_head", synth.Q6_K, 8192, 128256)
+N_LAYERS_70B = 80
+DISTINCT_70B = 8  # distinct layer weight sets, cycled over the 80 layers (4.3 GB, far above L2)
 
 
 def sweep_calls():
@@ -227,6 +234,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-shape, prefill and e2e passes")
+    ap.add_argument("--workload", default="8b", choices=["8b", "70b"],
+                    help="8b: the decode sweep (headline, replicas per GPU); 70b: BASELINE config 5, every "
+                         "matrix row-sharded over the GPUs with the fused all-gather")
     ap.add_argument("--shape", default=None,
                     help="profiling case TYPE:K:N:M (e.g. Q4_K:4096:14336:1): run only that matmul_quant "
                          "--steps times after --warmup, and print its timing")
@@ -236,6 +246,8 @@ def main():
         return run_reference_arm(args)
     if args.shape:
         return run_shape(args)
+    if args.workload == "70b":
+        return run_70b(args)
 
     import torch
 
@@ -375,6 +387,9 @@ def main():
             "gemv_tok_s": round(1e3 / ms_step, 2),
             "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(), "plan_q4k_gate": plan_q4k}
+    if dist is not None:
+        # BASELINE config 5 at this GPU count: the row-sharded 70B sweep
+        line["sharded_70b"] = measure_70b(torch, dist, dev, world, rank, args.steps, args.warmup)
     line.update({k: v for k, v in extra.items() if k != "e2e"})
     if "e2e" in extra:
         line["e2e"] = extra["e2e"]
@@ -382,6 +397,50 @@ def main():
         line["cpu_baseline"] = cpu_baseline()
     if dist is not None:
         dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
+def run_70b(args):
+    """--workload 70b: BASELINE config 5 as the bench line (any GPU count; a
+    one-process group at N=1)."""
+    import datetime
+    import socket
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world == 1 and "MASTER_PORT" not in os.environ:
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    with ClockSampler(local) as clocks:
+        r = measure_70b(torch, dist, dev, world, rank, args.steps, args.warmup)
+    peak, peak_kind = measured_peaks()
+    line = {"metric": "70B decode sweep, row-sharded: weight+activation GB/s (whole job); tok/s",
+            "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x int4/int6 -> int32 (dp4a), fp32 scales",
+            "data": "synthetic (seeded GGML Q4_K/Q6_K blocks, N(0,1) fp32 activations)",
+            "config": {"workload": r["workload"], "layers": N_LAYERS_70B, "distinct_layers": DISTINCT_70B,
+                       "calls_per_step": r["calls_per_step"], "bytes_per_step": r["bytes_per_step"],
+                       "l2": "inputs larger than L2 (8 distinct layers = 4.3 GB, cycled)",
+                       "parallelism": f"row-sharded over {world} GPU(s)"},
+            "tok_s": r["tok_s"], "pct_of_peak": round(100.0 * r["value"] / world / peak, 2),
+            "peak_source": peak_kind, "first_8_layers_ms": r["first_8_layers_ms"], "gather": r["gather"],
+            "clocks": clocks.summary()}
+    dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line))
     return 0
@@ -422,6 +481,75 @@ def run_shape(args):
                       "bytes": call_bytes(t, k, n, m), "plan": list(info),
                       "note": "eager back-to-back launches (includes launch gaps)"}))
     return 0
+
+
+def measure_70b(torch, dist, dev, world, rank, steps, warmup):
+    """BASELINE config 5 on `world` GPUs: one decode sweep of the 70B shapes
+    (80 layers x 7 projections + lm_head = 561 matmul_quant calls, M=1) with
+    every matrix row-sharded, each call's output all-gathered by the GEMV's own
+    peer stores plus one signal barrier (RowShardGroup.matmul).  Returns the
+    whole-job numbers (max over ranks) and, on the first 8 layers, the same
+    calls through the local GEMV + NCCL all_gather_into_tensor baseline."""
+    from cllm_inference_b200 import sharded
+
+    grp = sharded.RowShardGroup(max_out=LM_HEAD_70B[3], max_rows=1)
+    w = {}
+    for d in range(DISTINCT_70B):
+        for (name, t, k, n) in LAYER_70B:
+            _, rows = sharded.shard_rows(n, world, rank)
+            data = synth.make_weights_torch(t, rows, k, seed=7000 + 100 * d + len(name) * 7 + n + rank, device=dev)
+            w[(d, name)] = sharded.ShardedWeight(data, t, k, n, world, rank)
+    name, t, k, n = LM_HEAD_70B
+    _, rows = sharded.shard_rows(n, world, rank)
+    w[(0, name)] = sharded.ShardedWeight(synth.make_weights_torch(t, rows, k, seed=9001 + rank, device=dev),
+                                         t, k, n, world, rank)
+    xs = {k: torch.from_numpy(synth.make_activations(1, k, k + 1)).to(dev) for k in (8192, 28672)}
+    calls = [(l % DISTINCT_70B, p[0]) for l in range(N_LAYERS_70B) for p in LAYER_70B] + [(0, name)]
+    step_bytes = sum(synth.row_bytes(w[c].type, w[c].in_dim) * w[c].out_dim + 4 * (w[c].in_dim + w[c].out_dim)
+                     for c in calls)
+
+    def run(cs, nccl=False):
+        for c in cs:
+            sw = w[c]
+            if nccl:
+                grp.matmul_nccl(xs[sw.in_dim], sw, 1)
+            else:
+                grp.matmul_unread(xs[sw.in_dim], sw, 1)
+
+    def timed(g, reps):
+        for _ in range(max(warmup, 1)):
+            g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        tt = torch.tensor([a.elapsed_time(b) / reps], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    g = capture_graph(torch, lambda: run(calls))
+    ms = timed(g, steps)
+    part = calls[:DISTINCT_70B * len(LAYER_70B)]
+    g8 = capture_graph(torch, lambda: run(part))
+    ms8 = timed(g8, steps)
+    g8n = capture_graph(torch, lambda: run(part, nccl=True))
+    ms8n = timed(g8n, steps)
+    torch.cuda.synchronize()
+    from cllm_inference_b200 import _lib
+
+    _lib.check(_lib.load().cllm_cuda_check_device_status())
+    del g, g8, g8n
+    grp.close()
+    return {"workload": "Llama-3-70B decode sweep (BASELINE config 5), M=1, row-sharded",
+            "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "tok_s": round(1e3 / ms, 2), "bytes_per_step": step_bytes, "calls_per_step": len(calls),
+            "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings) + signal barrier",
+            "first_8_layers_ms": {"fused_peer_stores": round(ms8, 4), "nccl_all_gather": round(ms8n, 4)}}
 
 
 def capture_graph(torch, fn):

@@ -128,6 +128,16 @@ class RowShardGroup:
         """y = W x for the full W (every rank gets all out_dim outputs).  x:
         [n_rows, in_dim] fp32 on this GPU, the same on every rank; bias: full
         out_dim fp32 or None.  Returns [n_rows, out_dim] (a copy, or `out`)."""
+        y = self.matmul_unread(x, sw, n_rows, bias)
+        if out is None:
+            return y.clone()
+        out.copy_(y)
+        return out
+
+    def matmul_unread(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
+        """matmul without the copy-out: returns a view of the group's y buffer,
+        valid until the call after next overwrites it (for benchmarks and for
+        callers that consume y before issuing two more calls)."""
         import torch
 
         if n_rows > self.max_rows or sw.out_dim > self.max_out:
@@ -139,13 +149,10 @@ class RowShardGroup:
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
             ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, sw.in_dim, sw.out_dim,
             self.rank, self.world, n_rows, self._yptrs[buf], st))
-        _lib.check(self.lib.cllm_cuda_shard_barrier(self._sigptrs, ctypes.c_void_p(self._epoch.data_ptr()),
-                                                    self.world, self.rank, st))
-        y = self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
-        if out is None:
-            return y.clone()
-        out.copy_(y)
-        return out
+        if self.world > 1:  # one GPU: stream order alone completes y
+            _lib.check(self.lib.cllm_cuda_shard_barrier(self._sigptrs, ctypes.c_void_p(self._epoch.data_ptr()),
+                                                        self.world, self.rank, st))
+        return self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
 
     def matmul_nccl(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
         """The same result through the local GEMV and an NCCL all-gather."""
