@@ -186,7 +186,7 @@ GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
 
 constexpr uint32_t kSmemPerCta = 110 * 1024;  // two CTAs per SM
 constexpr uint32_t kTileTarget = 32 * 1024;   // bytes of weights per tile
-constexpr uint32_t kFusedActMax = 40 * 1024;  // largest quantized activation kept in shared memory
+constexpr uint32_t kFusedActMax = 48 * 1024;  // largest quantized activation kept in shared memory (M=1, K <= 32768)
 
 struct GemvPlan {
     bool tma, fused;

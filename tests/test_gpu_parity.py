@@ -192,7 +192,13 @@ LAYER_SHAPES = [("q/o", synth.Q4_K, 4096, 4096), ("k/v", synth.Q4_K, 4096, 1024)
                 ("q5_k", synth.Q5_K, 4096, 4096)]
 
 
-@pytest.mark.parametrize("name,t,k,n", LAYER_SHAPES, ids=[s[0] for s in LAYER_SHAPES])
+# BASELINE config 5 (70B) projections whose in_dim exceeds the 8B ones: the
+# fused quantization holds up to 32768 activation values per row.
+LAYER_SHAPES_70B = [("70b-gate/up", synth.Q4_K, 8192, 28672), ("70b-down", synth.Q6_K, 28672, 8192)]
+
+
+@pytest.mark.parametrize("name,t,k,n", LAYER_SHAPES + LAYER_SHAPES_70B,
+                         ids=[s[0] for s in LAYER_SHAPES + LAYER_SHAPES_70B])
 def test_baseline_layer_shapes(cuda, lib, oracle, name, t, k, n):
     w = synth.make_weights(t, n, k, seed=n + k + t)
     x = synth.make_activations(4, k, seed=k)
