@@ -514,7 +514,9 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
             if nccl:
                 grp.matmul_nccl(xs[sw.in_dim], sw, 1)
             else:
-                grp.matmul_unread(xs[sw.in_dim], sw, 1)
+                grp.matmul_unread(xs[sw.in_dim], sw, 1, chain=True)
+        if not nccl:
+            grp.sync()
 
     def timed(g, reps):
         for _ in range(max(warmup, 1)):
@@ -548,7 +550,8 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
     return {"workload": "Llama-3-70B decode sweep (BASELINE config 5), M=1, row-sharded",
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "tok_s": round(1e3 / ms, 2), "bytes_per_step": step_bytes, "calls_per_step": len(calls),
-            "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings) + signal barrier",
+            "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings); its last warp "
+                                     "signals every rank; the next call waits for all signals",
             "first_8_layers_ms": {"fused_peer_stores": round(ms8, 4), "nccl_all_gather": round(ms8n, 4)}}
 
 

@@ -26,6 +26,8 @@ ERR_KERNEL_TIMEOUT = -7
 ERR_TOO_LARGE = -8
 
 X_HOST, Y_HOST, W_HOST = 1, 2, 4
+SHARD_WAIT_PREV = 1
+SHARD_PAD_WORDS = 16
 HOST_IO = X_HOST | Y_HOST
 
 _P = ctypes.c_void_p
@@ -51,7 +53,9 @@ SIGNATURES = {
     "cllm_cuda_matmul_plan": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_I), _I]),
     "cllm_cuda_matmul_quant_noalloc": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _P]),
     "cllm_cuda_shard_rows": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
-    "cllm_cuda_matmul_quant_rowshard": (_I, [_P, _P, _I, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_P), _P]),
+    "cllm_cuda_matmul_quant_rowshard": (_I, [_P, _P, _I, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_P),
+                                             ctypes.POINTER(_P), _P, _U, _P]),
+    "cllm_cuda_shard_wait": (_I, [_P, _P, _I, _P]),
     "cllm_cuda_shard_barrier": (_I, [ctypes.POINTER(_P), _P, _I, _I, _P]),
     "cllm_cuda_check_device_status": (_I, []),
     "cllm_cuda_last_error": (_I, [ctypes.c_char_p, _SZ]),

@@ -440,6 +440,23 @@ int noalloc_scratch(int dev, uint8_t** out) {
 
 using namespace cllm;
 
+// PDL launch of a one-warp shard kernel.
+template <class... Args>
+int launch_shard_kernel(void (*kern)(Args...), cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
 extern "C" {
 
 int cllm_cuda_last_error(char* buf, size_t n) {
@@ -822,11 +839,16 @@ int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* 
 
 int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int type, const float* bias,
                                     int in_dim, int out_dim, int rank, int world, int n_rows,
-                                    float* const* y_peers, void* stream) {
+                                    float* const* y_peers, uint32_t* const* signal_pads, uint32_t* epoch,
+                                    unsigned flags, void* stream) {
     const char* fname = "matmul_quant_rowshard";
     if (n_rows <= 0) return CLLM_OK;
     if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !y_peers)
         return fail(CLLM_ERR_INVALID_ARG, "%s: bad group (world %d, rank %d)", fname, world, rank);
+    if (flags & ~CLLM_SHARD_WAIT_PREV) return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
+    if (signal_pads && !epoch) return fail(CLLM_ERR_INVALID_ARG, "%s: signal pads without an epoch word", fname);
+    if ((flags & CLLM_SHARD_WAIT_PREV) && !signal_pads)
+        return fail(CLLM_ERR_INVALID_ARG, "%s: CLLM_SHARD_WAIT_PREV needs the signal pads", fname);
     if (n_rows > 8) return fail(CLLM_ERR_TOO_LARGE, "%s: at most 8 activation rows (got %d)", fname, n_rows);
     if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
     const int bsz = block_size_of(type);
@@ -834,10 +856,23 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
     int row0, rows;
     shard_rows(out_dim, world, rank, &row0, &rows);
-    for (int q = 0; q < world; ++q)
+    for (int q = 0; q < world; ++q) {
         if (!y_peers[q]) return fail(CLLM_ERR_INVALID_ARG, "%s: null y buffer of rank %d", fname, q);
-    if (rows == 0) return CLLM_OK;
-    if (in_dim > 0 && (!x || !w_shard)) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+        if (signal_pads && !signal_pads[q])
+            return fail(CLLM_ERR_INVALID_ARG, "%s: null signal pad of rank %d", fname, q);
+    }
+    if (rows == 0) {  // nothing to compute; still announce the round
+        if (!signal_pads) return CLLM_OK;
+        ShardSignal sg{};
+        for (int q = 0; q < world; ++q) sg.pads[q] = signal_pads[q];
+        sg.epoch = epoch;
+        sg.world = world;
+        sg.rank = rank;
+        int dev;
+        if (int rc = ensure_device(&dev)) return rc;
+        return launch_shard_kernel(shard_signal_kernel, static_cast<cudaStream_t>(stream), sg);
+    }
+    if (rows > 0 && in_dim > 0 && (!x || !w_shard)) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
     int dev;
     if (int rc = ensure_device(&dev)) return rc;
     const DeviceInfo& di = g_dev[dev];
@@ -851,6 +886,12 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, n_rows, true, di, x);
     pl.num_tiles = (rows + pl.rows_per_tile - 1) / pl.rows_per_tile;
     pl.grid = std::max(1, std::min(pl.grid, pl.num_tiles));
+    const bool wait_prev = (flags & CLLM_SHARD_WAIT_PREV) != 0;
+    if (wait_prev && !pl.fused) {  // x is read by the quantize kernel: wait before it
+        if (int rc = launch_shard_kernel(shard_wait_kernel, st, (const uint32_t*)signal_pads[rank],
+                                         (const uint32_t*)epoch, world))
+            return rc;
+    }
     uint8_t* ws = nullptr;
     if (!pl.fused) {
         if (int rc = workspace(dev, L.end, &ws)) return rc;
@@ -874,12 +915,26 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     p.ldy = out_dim;
     p.npeers = world;
     for (int q = 0; q < world; ++q) p.ypeers[q] = y_peers[q] + row0;
+    if (signal_pads) {
+        for (int q = 0; q < world; ++q) p.spads[q] = signal_pads[q];
+        p.sepoch = epoch;
+        p.srank = rank;
+        p.swait = (wait_prev && pl.fused) ? 1 : 0;
+    }
     if (!pl.fused) {
         if (int rc = launch_quantize(x, in_dim, n_rows, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
                                      const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
             return rc;
     }
     return launch_gemv(type, false, n_rows, pl, p, st);
+}
+
+int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int world, void* stream) {
+    if (world < 1 || world > kMaxPeers || !own_pad || !epoch)
+        return fail(CLLM_ERR_INVALID_ARG, "shard_wait: bad arguments (world %d)", world);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    return launch_shard_kernel(shard_wait_kernel, static_cast<cudaStream_t>(stream), own_pad, epoch, world);
 }
 
 int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream) {
@@ -895,9 +950,7 @@ int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int w
     sg.rank = rank;
     int dev;
     if (int rc = ensure_device(&dev)) return rc;
-    shard_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(sg);
-    CLLM_CUDA_TRY(cudaGetLastError());
-    return CLLM_OK;
+    return launch_shard_kernel(shard_barrier_kernel, static_cast<cudaStream_t>(stream), sg);
 }
 
 int cllm_cuda_check_device_status(void) {

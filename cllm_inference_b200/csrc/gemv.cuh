@@ -23,6 +23,8 @@
 namespace cllm {
 
 constexpr int kMaxPeers = 8;  // GPUs of one node that a row-sharded call writes to
+constexpr int kShardPadWords = 16;
+constexpr int kShardCountSlot = kMaxPeers;
 
 struct GemvParams {
     const uint8_t* w;     // weight matrix, out_dim rows of row_bytes
@@ -45,6 +47,13 @@ struct GemvParams {
     int64_t ldy;          // row stride of y (0: N); set per launch
     int npeers;           // > 0: row-sharded call, y goes to every ypeers[q] instead of y
     float* ypeers[kMaxPeers];
+    // row-sharded completion signalling (spads[0] == nullptr: none).  Signal
+    // pads: kShardPadWords uint32 per rank, peer-mapped; slot q = the last
+    // epoch rank q completed, slot kShardCountSlot = this rank's arrival count.
+    uint32_t* spads[kMaxPeers];
+    uint32_t* sepoch;     // this rank's epoch word (last completed round)
+    int srank;
+    int swait;            // wait for every rank to have completed *sepoch before reading x
 };
 
 constexpr int kGemvWarps = 8;                      // warps that compute (R rows x wpr warps per row)
@@ -697,6 +706,45 @@ __device__ __forceinline__ void gemv_store_partial(float* red, int warp, const f
 }
 
 // y = sum of the wpr warp partials of each row (in warp order) + bias.
+// Row-sharded call, start: wait until every rank has completed the epoch in
+// *sepoch (the previous round), so that x -- typically the previous call's
+// all-gathered y -- is complete.  Threads 0..npeers-1 poll; bounded.
+__device__ __forceinline__ void shard_wait_prev(const GemvParams& p) {
+    const int q = threadIdx.x;
+    if (q < p.npeers) {
+        const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(p.sepoch);
+        const uint32_t* slot = p.spads[p.srank] + q;
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(slot) : "memory");
+            if ((int32_t)(v - ep) >= 0) break;
+            if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(&g_device_status, kStatusTimeout);
+                break;
+            }
+        }
+    }
+}
+
+// Row-sharded call, end: one arrival per CTA, by thread 0 after the CTA's
+// compute threads have synchronized (gpu-scope fence: the arrival count is
+// local); the grid's last CTA orders everything system-wide and announces
+// the new epoch to every rank, then resets the count.
+__device__ __forceinline__ void shard_arrive_cta(const GemvParams& p) {
+    if (threadIdx.x != 0) return;
+    __threadfence();
+    uint32_t* count = p.spads[p.srank] + kShardCountSlot;
+    if (atomicAdd(count, 1u) == gridDim.x - 1u) {
+        __threadfence_system();
+        const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(p.sepoch) + 1u;
+        for (int q = 0; q < p.npeers; ++q)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.spads[q] + p.srank), "r"(ep) : "memory");
+        *reinterpret_cast<volatile uint32_t*>(p.sepoch) = ep;
+        *reinterpret_cast<volatile uint32_t*>(count) = 0u;
+    }
+}
+
 // Store y[t][j]: locally, or (row-sharded call) into the y buffer of every GPU
 // of the group over NVLink peer mappings, so the output is all-gathered as it
 // is produced.
@@ -897,6 +945,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
 
     // ---- compute warps: activations are read after the previous kernel is done
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (FUSED && p.spads[0] && p.swait) {  // (unfused: the host waits before the quantize kernel)
+        shard_wait_prev(p);
+        named_barrier_sync(kGemvThreads);
+    }
     uint32_t quirk;
     ActSmem<TYPE> as{};
     ActGmem ag{p.qx, p.dx, p.bs, p.K, nb};
@@ -957,9 +1009,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * stg);
     }
-    // row-sharded call: this thread's peer stores are visible system-wide before
-    // the kernel ends (the barrier kernel that follows announces them)
-    if (p.npeers > 0) __threadfence_system();
+    if (p.spads[0]) {
+        named_barrier_sync(kGemvThreads);
+        shard_arrive_cta(p);
+    }
 }
 
 template <int TYPE, int M, bool EMIT>
@@ -987,7 +1040,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_direct_kernel(const GemvPar
             __syncthreads();
         }
     }
-    if (p.npeers > 0) __threadfence_system();
+    if (p.spads[0]) {
+        __syncthreads();
+        shard_arrive_cta(p);
+    }
 }
 
 }  // namespace cllm

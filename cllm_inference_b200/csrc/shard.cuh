@@ -22,7 +22,14 @@ struct ShardSignal {
 
 // One warp.  The epoch lives in device memory so that a CUDA graph that
 // replays the barrier advances it on every replay.
+// Launched as a programmatic dependent of the GEMV: it may be resident early,
+// waits for the GEMV's completion (griddepcontrol.wait), then lets the next
+// kernel in the stream launch and prefetch its weights while it signals.  The
+// system-scope fence before each release store orders the GEMV's peer stores
+// (which happen before this kernel's wait returns) ahead of the signal.
 __global__ void __launch_bounds__(32) shard_barrier_kernel(const ShardSignal s) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int q = threadIdx.x;
     const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(s.epoch) + 1u;
     __syncwarp();
@@ -41,6 +48,44 @@ __global__ void __launch_bounds__(32) shard_barrier_kernel(const ShardSignal s) 
                 break;
             }
         }
+    }
+    __syncwarp();
+    if (q == 0) *s.epoch = ep;
+}
+
+// Wait (bounded) until every rank has completed the round in *epoch: the
+// last warp of each rank's row-sharded GEMV announced it into slot `rank` of
+// every pad.  Launched as a programmatic dependent of that GEMV.
+__global__ void __launch_bounds__(32) shard_wait_kernel(const uint32_t* pad, const uint32_t* epoch, int world) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int q = threadIdx.x;
+    if (q < world) {
+        const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(epoch);
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(pad + q) : "memory");
+            if ((int32_t)(v - ep) >= 0) break;
+            if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(&g_device_status, kStatusTimeout);
+                break;
+            }
+        }
+    }
+}
+
+// A rank that owns no row of a row-sharded call: announce the round like the
+// GEMV's last warp would, without launching a GEMV.
+__global__ void __launch_bounds__(32) shard_signal_kernel(const ShardSignal s) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int q = threadIdx.x;
+    const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(s.epoch) + 1u;
+    __syncwarp();
+    if (q < s.world) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(s.pads[q] + s.rank), "r"(ep) : "memory");
     }
     __syncwarp();
     if (q == 0) *s.epoch = ep;

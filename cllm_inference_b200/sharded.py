@@ -10,9 +10,10 @@ Two ways to gather the slices:
 
 * ``RowShardGroup.matmul`` -- the product path.  The GEMV stores each output
   element straight into the y buffer of every rank (NVLink peer mappings of
-  symmetric memory), then one small barrier kernel exchanges a release/acquire
-  signal per pair of GPUs (``cllm_cuda_matmul_quant_rowshard`` +
-  ``cllm_cuda_shard_barrier``).  No separate collective runs.
+  symmetric memory); its last warp announces the round to every rank with a
+  release store, and the next call (or ``sync``) waits for all announcements
+  before it reads its input (``cllm_cuda_matmul_quant_rowshard``,
+  ``cllm_cuda_shard_wait``).  No separate collective runs.
 * ``RowShardGroup.matmul_nccl`` -- the baseline: the local GEMV, then
   ``all_gather_into_tensor`` over NCCL and a reorder (``gather_rows``).
 
@@ -134,10 +135,13 @@ class RowShardGroup:
         out.copy_(y)
         return out
 
-    def matmul_unread(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
+    def matmul_unread(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None, chain: bool = False):
         """matmul without the copy-out: returns a view of the group's y buffer,
-        valid until the call after next overwrites it (for benchmarks and for
-        callers that consume y before issuing two more calls)."""
+        valid until the call after next overwrites it.  Each call first waits
+        (on the GPU) for every rank to have finished the previous call, so x
+        may be the previous call's output.  chain=True skips the wait for this
+        call's own completion: its y may then only be read by the next call of
+        this group (or after sync())."""
         import torch
 
         if n_rows > self.max_rows or sw.out_dim > self.max_out:
@@ -145,14 +149,24 @@ class RowShardGroup:
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         buf = self._flip
         self._flip ^= 1
+        solo = self.world == 1  # one GPU: stream order alone completes y
         _lib.check(self.lib.cllm_cuda_matmul_quant_rowshard(
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
             ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, sw.in_dim, sw.out_dim,
-            self.rank, self.world, n_rows, self._yptrs[buf], st))
-        if self.world > 1:  # one GPU: stream order alone completes y
-            _lib.check(self.lib.cllm_cuda_shard_barrier(self._sigptrs, ctypes.c_void_p(self._epoch.data_ptr()),
-                                                        self.world, self.rank, st))
+            self.rank, self.world, n_rows, self._yptrs[buf], None if solo else self._sigptrs,
+            None if solo else ctypes.c_void_p(self._epoch.data_ptr()), 0 if solo else _lib.SHARD_WAIT_PREV, st))
+        if not chain:
+            self.sync()
         return self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
+
+    def sync(self):
+        """Wait on the GPU until every rank has finished the last call."""
+        import torch
+
+        if self.world > 1:
+            st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            _lib.check(self.lib.cllm_cuda_shard_wait(ctypes.c_void_p(self._sig.data_ptr()),
+                                                     ctypes.c_void_p(self._epoch.data_ptr()), self.world, st))
 
     def matmul_nccl(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
         """The same result through the local GEMV and an NCCL all-gather."""

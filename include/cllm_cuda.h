@@ -177,17 +177,36 @@ int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* 
  * output is all-gathered by the GEMV's own stores.  x: [n_rows][in_dim] fp32
  * on this device (the full activation, the same on every rank); w_shard:
  * this rank's rows only (rows x row_bytes, native blocks, device memory);
- * bias: the full out_dim bias or NULL.  n_rows <= 8.  Asynchronous: y is
- * complete on a rank only after cllm_cuda_shard_barrier. */
+ * bias: the full out_dim bias or NULL.  n_rows <= 8.
+ *
+ * Completion.  signal_pads (NULL: none) are every rank's signal pads
+ * (CLLM_SHARD_PAD_WORDS zero-initialised uint32 each, peer-mapped) and epoch
+ * this rank's zero-initialised epoch word: the call's last warp then
+ * announces "this rank's slice of round epoch+1 has landed" to every rank
+ * and advances *epoch.  y is complete on a rank once every rank has
+ * announced the round: cllm_cuda_shard_wait waits for that, and a following
+ * row-sharded call given CLLM_SHARD_WAIT_PREV waits for it before it reads
+ * its x (so chained projections need no separate wait).  Without signal
+ * pads, use cllm_cuda_shard_barrier.  Every rank must make the same sequence
+ * of signalling calls.  A rank whose slice is empty still signals. */
+#define CLLM_SHARD_PAD_WORDS 16
+#define CLLM_SHARD_WAIT_PREV 1u
 int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int type, const float* bias,
                                     int in_dim, int out_dim, int rank, int world, int n_rows,
-                                    float* const* y_peers, void* stream);
+                                    float* const* y_peers, uint32_t* const* signal_pads, uint32_t* epoch,
+                                    unsigned flags, void* stream);
+
+/* Wait (on the GPU, bounded: 1 s, then the device status reports
+ * CLLM_ERR_KERNEL_TIMEOUT) until every rank has announced the round in
+ * *epoch into own_pad (this rank's signal pad). */
+int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int world, void* stream);
 
 /* Completion barrier of a row-sharded call: tells every rank that this
  * rank's slice has landed (a release store of the new epoch into slot `rank`
  * of signal_pads[q], q < world) and waits until every rank has reached the
- * same epoch (slot q of signal_pads[rank]).  signal_pads: each rank's
- * zero-initialised array of >= world uint32 words, peer-mapped; epoch: this
+ * same epoch (slot q of signal_pads[rank]), for row-sharded calls made
+ * without signal pads.  signal_pads: each rank's zero-initialised pad of
+ * CLLM_SHARD_PAD_WORDS uint32, peer-mapped; epoch: this
  * rank's own zero-initialised device word, advanced by one per barrier on the
  * GPU (so a CUDA graph that replays the barrier stays in step).  Every rank
  * must run the same sequence of barriers.  The wait is bounded (1 s): a

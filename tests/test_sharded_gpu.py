@@ -58,7 +58,7 @@ def test_rowshard_emulated_ranks(lib, case, world):
     for rank in range(world):
         part = to_dev(np.ascontiguousarray(sharded.shard_weight_bytes(w, t, k, n, world, rank)))
         _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(part), t, dptr(bias), k, n, rank, world, m,
-                                                       _ptrs(ys), stream()))
+                                                       _ptrs(ys), None, None, 0, stream()))
     torch.cuda.synchronize()
     _lib.check(lib.cllm_cuda_check_device_status())
     for y in ys:  # every rank's buffer holds every slice, bit-identical to one GPU
@@ -112,9 +112,86 @@ def test_rowshard_rejects_bad_groups(lib):
     w = torch.zeros(144, dtype=torch.uint8, device="cuda")
     for rank, world in ((0, 0), (0, 9), (2, 2)):
         assert lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(w), synth.Q4_K, None, 256, 1, rank, world, 1,
-                                                   _ptrs([y] * max(world, 1)), stream()) == _lib.ERR_INVALID_ARG
+                                                   _ptrs([y] * max(world, 1)), None, None, 0,
+                                                   stream()) == _lib.ERR_INVALID_ARG
     assert lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(w), synth.Q4_K, None, 256, 1, 0, 1, 9,
-                                               _ptrs([y]), stream()) == _lib.ERR_TOO_LARGE
+                                               _ptrs([y]), None, None, 0, stream()) == _lib.ERR_TOO_LARGE
+    # waiting on the previous round needs the signal pads
+    assert lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(w), synth.Q4_K, None, 256, 1, 0, 1, 1,
+                                               _ptrs([y]), None, None, _lib.SHARD_WAIT_PREV,
+                                               stream()) == _lib.ERR_INVALID_ARG
+
+
+def _pads(world):
+    return [torch.zeros(_lib.SHARD_PAD_WORDS, dtype=torch.int32, device="cuda") for _ in range(world)]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rowshard_signals_every_rank(lib, world):
+    """Each emulated rank's call announces its round into every pad and
+    resets its arrival count; once all ranks have run, each rank's wait
+    passes, and the next round (CLLM_SHARD_WAIT_PREV) sees the previous one
+    complete.  Ranks run one after another: nothing waits on a later launch."""
+    t, k, n, m = synth.Q4_K, 4096, 300, 1
+    w = synth.make_weights(t, n, k, seed=9)
+    x = to_dev(synth.make_activations(m, k, 3))
+    ref = _full(lib, x, to_dev(w), t, k, n, m)
+    pads = _pads(world)
+    epochs = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(world)]
+    parts = [to_dev(np.ascontiguousarray(sharded.shard_weight_bytes(w, t, k, n, world, r))) for r in range(world)]
+    for rnd in range(1, 3):
+        ys = [torch.full((m, n), float("nan"), device="cuda") for _ in range(world)]
+        for r in range(world):
+            _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(parts[r]), t, None, k, n, r, world, m,
+                                                           _ptrs(ys), _ptrs(pads), dptr(epochs[r]),
+                                                           _lib.SHARD_WAIT_PREV, stream()))
+        for r in range(world):
+            _lib.check(lib.cllm_cuda_shard_wait(dptr(pads[r]), dptr(epochs[r]), world, stream()))
+        torch.cuda.synchronize()
+        _lib.check(lib.cllm_cuda_check_device_status())
+        for r in range(world):
+            assert int(epochs[r].item()) == rnd
+            assert pads[r][:world].tolist() == [rnd] * world
+            assert int(pads[r][_lib.SHARD_PAD_WORDS // 2].item()) == 0  # arrival count reset
+            assert torch.equal(ys[r], ref)
+
+
+def test_rowshard_empty_slice_still_signals(lib):
+    """More ranks than rows: rank 2 of 3 owns no row of a 2-row matrix, yet its
+    call announces the round, so the others' waits do not run out."""
+    t, k, n, world = synth.Q8_0, 256, 2, 3
+    w = synth.make_weights(t, n, k, seed=4)
+    x = to_dev(synth.make_activations(1, k, 6))
+    pads, ys = _pads(world), [torch.zeros((1, n), device="cuda") for _ in range(world)]
+    epochs = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(world)]
+    for r in range(world):
+        part = to_dev(np.ascontiguousarray(sharded.shard_weight_bytes(w, t, k, n, world, r)))
+        _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(part) if part.numel() else dptr(x), t, None,
+                                                       k, n, r, world, 1, _ptrs(ys), _ptrs(pads),
+                                                       dptr(epochs[r]), 0, stream()))
+    _lib.check(lib.cllm_cuda_shard_wait(dptr(pads[0]), dptr(epochs[0]), world, stream()))
+    torch.cuda.synchronize()
+    _lib.check(lib.cllm_cuda_check_device_status())
+    assert pads[0][:world].tolist() == [1, 1, 1]
+    assert torch.equal(ys[0], _full(lib, x, to_dev(w), t, k, n, 1))
+
+
+def test_rowshard_wait_for_missing_rank_times_out(lib):
+    """CLLM_SHARD_WAIT_PREV while a peer never finished the previous round:
+    the in-kernel wait gives up after its bound, the status reports it, and
+    the call still completes (no fault, no hang)."""
+    t, k, n, world = synth.Q4_K, 4096, 64, 2
+    w = synth.make_weights(t, n, k, seed=8)
+    x = to_dev(synth.make_activations(1, k, 1))
+    pads, ys = _pads(world), [torch.zeros((1, n), device="cuda") for _ in range(world)]
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    part = to_dev(np.ascontiguousarray(sharded.shard_weight_bytes(w, t, k, n, world, 0)))
+    for _ in range(2):  # round 1 completes locally; round 2 waits for rank 1's round 1, which never comes
+        _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(part), t, None, k, n, 0, world, 1, _ptrs(ys),
+                                                       _ptrs(pads), dptr(epoch), _lib.SHARD_WAIT_PREV, stream()))
+    torch.cuda.synchronize()
+    assert lib.cllm_cuda_check_device_status() == _lib.ERR_KERNEL_TIMEOUT
+    assert int(epoch.item()) == 2
 
 
 def _free_port():
