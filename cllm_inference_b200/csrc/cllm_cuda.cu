@@ -184,6 +184,63 @@ GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
     return nullptr;
 }
 
+typedef void (*ImageFn)(const float*, int, uint8_t*);
+
+template <int T>
+ImageFn image_fn(int m) {
+    switch (m) {
+        case 1: return act_image_kernel<1, T>;
+        case 2: return act_image_kernel<2, T>;
+        case 3: return act_image_kernel<3, T>;
+        case 4: return act_image_kernel<4, T>;
+        case 5: return act_image_kernel<5, T>;
+        case 6: return act_image_kernel<6, T>;
+        case 7: return act_image_kernel<7, T>;
+        case 8: return act_image_kernel<8, T>;
+    }
+    return nullptr;
+}
+
+ImageFn select_image(int type, int m) {
+    switch (type) {
+        case kQ4_0: return image_fn<kQ4_0>(m);
+        case kQ5_0: return image_fn<kQ5_0>(m);
+        case kQ8_0: return image_fn<kQ8_0>(m);
+        case kQ4_K: return image_fn<kQ4_K>(m);
+        case kQ5_K: return image_fn<kQ5_K>(m);
+        case kQ6_K: return image_fn<kQ6_K>(m);
+    }
+    return nullptr;
+}
+
+// Fused GEMVs with at least this many activation values per row get their
+// activations quantized once (act_image_kernel) instead of in every CTA: the
+// per-CTA copy of x (4 bytes per value, read by ~300 CTAs) and its
+// quantization would otherwise dominate the call.
+constexpr int kImageMinK = 8192;
+
+uint32_t image_bytes(int m, int K) { return (uint32_t)kImageHeader + fused_act_bytes(m, K); }
+
+// Launch act_image_kernel for m rows of x (programmatic dependent launch).
+int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas, cudaStream_t st) {
+    ImageFn fn = select_image(type, m);
+    if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no activation-image kernel for type %d, %d rows", type, m);
+    const int groups = (m * (K / 32) + kGemvThreads / 4 - 1) / (kGemvThreads / 4);
+    const int n = std::max(1, std::min(kImageMaxCtas, groups));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img));
+    *ctas = n;
+    return CLLM_OK;
+}
+
 constexpr uint32_t kSmemPerCta = 110 * 1024;  // two CTAs per SM
 constexpr uint32_t kTileTarget = 32 * 1024;   // bytes of weights per tile
 constexpr uint32_t kFusedActMax = 48 * 1024;  // largest quantized activation kept in shared memory (M=1, K <= 32768)
@@ -594,6 +651,9 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
     }
     const size_t off_pre = total;
     if (use_tc) total += prefill_bytes(n_rows, in_dim);
+    const size_t off_img = total;
+    const bool want_image = !use_tc && in_dim >= kImageMinK;
+    if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
     uint8_t* ws;
     if (int rc = workspace(dev, total, &ws)) return rc;
 
@@ -635,6 +695,11 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
             if (int rc = launch_quantize(p.x, in_dim, m, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
                                          const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
                 return rc;
+        } else if (want_image && pl.tma) {
+            uint8_t* img = ws + off_img;
+            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st)) return rc;
+            p.image = img;
+            p.image_bytes = image_bytes(m, in_dim);
         }
         if (int rc = launch_gemv(type, false, m, pl, p, st)) return rc;
     }

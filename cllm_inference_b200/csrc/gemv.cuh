@@ -54,6 +54,12 @@ struct GemvParams {
     uint32_t* sepoch;     // this rank's epoch word (last completed round)
     int srank;
     int swait;            // wait for every rank to have completed *sepoch before reading x
+    // FUSED with image != nullptr: the activations were quantized by
+    // act_image_kernel into `image` (row masks, then the shared-memory layout);
+    // the producer copies it in instead of every CTA quantizing x itself.
+    const uint8_t* image;
+    uint32_t image_bytes;
+    int image_ctas;
 };
 
 constexpr int kGemvWarps = 8;                      // warps that compute (R rows x wpr warps per row)
@@ -66,6 +72,9 @@ constexpr int kHdrFull = 0;        // 8 x u64: "stage holds its tile" (tx-count 
 constexpr int kHdrEmpty = 64;      // 8 x u64: "every compute warp is done with the stage"
 constexpr int kHdrAbort = 128;     // int: a bounded wait expired
 constexpr int kHdrQuirk = 132;     // u32: per-row "activation holds -128" bits
+constexpr int kHdrImage = 136;     // u64: "the activation image has landed" (tx-count barrier)
+constexpr int kImageHeader = 128;  // image: u32 row masks of up to 32 quantizing CTAs, then the activations
+constexpr int kImageMaxCtas = kImageHeader / 4;
 constexpr int kHdrCount = 256;     // 8 stages x 8 rows of int: warps of a row that finished the tile
 constexpr int kHdrRed = 512;       // 8 stages x 8 warps x 8 floats: partial row sums
 
@@ -787,23 +796,23 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
 // every thread issues the loads of up to four blocks before reducing them.
 // x must be 16-byte aligned.  Returns the per-row "holds -128" mask.  Called
 // by all compute threads.
-template <int M, int TYPE>
-__device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
-                                                     uint8_t* qs, float* dx, int* bs, int* hs,
-                                                     uint32_t* s_quirk) {
+template <int M, int TYPE, bool GLOBAL>
+__device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x, int K, uint8_t* qs, float* dx,
+                                                    int* bs, int* hs, int gfirst, int gcount) {
+    // gfirst: this CTA's first group of blocks; gcount: groups per pass of all
+    // CTAs taking part (one CTA: 0 and 64).  Returns this thread's row mask.
     const int kp = act_row_stride(K);
     constexpr int kGroups = kGemvThreads / 4;  // 64 blocks per pass of the group loop
     constexpr int kUnroll = 4;
     const int g = threadIdx.x >> 2, sub = threadIdx.x & 3;
     const int nb = K >> 5;
     const int total = M * nb;
-    const uint32_t a_qs = smem_addr(qs);
     uint32_t mask = 0;
-    for (int base = 0; base < total; base += kGroups * kUnroll) {
+    for (int base = gfirst; base < total; base += gcount * kUnroll) {
         float4 v[kUnroll][2];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int blk = base + g + kGroups * u;
+            const int blk = base + g + gcount * u;
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
                 const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t * K + 32 * b + 8 * sub);
@@ -816,8 +825,8 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             // stop once no group of this warp has a block left (warp-uniform)
-            if (base + kGroups * u + (g & ~7) >= total) break;
-            const int blk = base + g + kGroups * u;  // uniform within each 4-lane group
+            if (base + gcount * u + (g & ~7) >= total) break;
+            const int blk = base + g + gcount * u;  // uniform within each 4-lane group
             const float vv[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
                                  v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
             // max of |x| over non-NaN values, as `if (a > amax) amax = a` from 0
@@ -851,8 +860,13 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
                 const int pb = act_perm<TYPE>(b, nb);
-                const uint32_t a = a_qs + (uint32_t)(t * kp) + act_swizzle(32u * pb + 8u * sub);
-                asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(w0), "r"(w1) : "memory");
+                const uint32_t off = (uint32_t)(t * kp) + act_swizzle(32u * pb + 8u * sub);
+                if constexpr (GLOBAL) {
+                    *reinterpret_cast<uint2*>(qs + off) = make_uint2(w0, w1);
+                } else {
+                    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(smem_addr(qs) + off), "r"(w0), "r"(w1)
+                                 : "memory");
+                }
                 // a byte equal to 0x80 (-128): zero byte of w ^ 0x80808080
                 const uint32_t z0 = w0 ^ 0x80808080u, z1 = w1 ^ 0x80808080u;
                 if (((z0 - 0x01010101u) & ~z0 & 0x80808080u) | ((z1 - 0x01010101u) & ~z1 & 0x80808080u))
@@ -865,12 +879,49 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
             }
         }
     }
+    (void)kGroups;
+    return mask;
+}
+
+template <int M, int TYPE>
+__device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
+                                                     uint8_t* qs, float* dx, int* bs, int* hs,
+                                                     uint32_t* s_quirk) {
+    const uint32_t mask = quantize_blocks<M, TYPE, false>(x, K, qs, dx, bs, hs, 0, kGemvThreads / 4);
     // OR over the compute warps (*s_quirk is zero on entry), then a barrier
     // over those warps only: the producer warp does not take part.
     const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
     if ((threadIdx.x & 31) == 0 && wm) atomicOr(s_quirk, wm);
     named_barrier_sync(kGemvThreads);
     return *reinterpret_cast<volatile uint32_t*>(s_quirk);
+}
+
+// Quantize x [M][K] once into an activation image in global memory: the
+// per-CTA row masks, then exactly the shared-memory layout the fused GEMV
+// builds (quantize_blocks), so each GEMV CTA copies it in with one bulk copy
+// instead of re-reading and re-quantizing x.  CTA c takes every gridDim.x-th
+// group of 64 blocks.  A programmatic dependent of the kernel that wrote x;
+// lets the GEMV launch (and start streaming weights) at once.
+template <int M, int TYPE>
+__global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __restrict__ x, int K,
+                                                                 uint8_t* __restrict__ image) {
+    __shared__ uint32_t s_mask;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) s_mask = 0;
+    __syncthreads();
+    const int nb = K >> 5;
+    uint8_t* qs = image + kImageHeader;
+    const uint32_t qbytes = (uint32_t)(M * act_row_stride(K));
+    float* dx = reinterpret_cast<float*>(qs + qbytes);
+    int* bs = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
+    int* hs = reinterpret_cast<int*>(qs + qbytes + 8u * (uint32_t)(M * nb));
+    const uint32_t mask = quantize_blocks<M, TYPE, true>(x, K, qs, dx, bs, hs, (int)blockIdx.x * (kGemvThreads / 4),
+                                                         (int)gridDim.x * (kGemvThreads / 4));
+    const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
+    if ((threadIdx.x & 31) == 0 && wm) atomicOr(&s_mask, wm);
+    __syncthreads();
+    if (threadIdx.x == 0) reinterpret_cast<uint32_t*>(image)[blockIdx.x] = s_mask;
 }
 
 // Shared-memory bytes the fused quantization needs for M rows of K.
@@ -908,6 +959,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kGemvWarps);
         }
+        mbar_init(sbase + kHdrImage, 1);
         *s_abort = 0;
         *s_quirk = 0;
         fence_mbar_init();
@@ -922,8 +974,18 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
     if (warp == kGemvWarps) {
         // ---- producer: weights are static, so no wait on the previous kernel
         if (lane == 0) {
+            // Image mode: two tiles of weights first (they do not depend on the
+            // previous kernel), then the activation image once it is written.
+            bool image_due = FUSED && p.image != nullptr;
+            auto issue_image = [&]() {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                mbar_arrive_expect_tx(sbase + kHdrImage, p.image_bytes);
+                bulk_g2s(sbase + kGemvSmemHeader - kImageHeader, p.image, p.image_bytes, sbase + kHdrImage);
+                image_due = false;
+            };
             int it = 0;
             for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+                if (image_due && it == 2) issue_image();
                 const int stg = it % S;
                 if (it >= S && !mbar_wait_or_abort(empty0 + 8 * stg, (uint32_t)((it / S) - 1) & 1u, s_abort))
                     break;
@@ -933,8 +995,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
                 mbar_arrive_expect_tx(full0 + 8 * stg, bytes);
                 bulk_g2s(ring + stg * p.stage_bytes, p.w + (int64_t)row0 * p.row_bytes, bytes, full0 + 8 * stg);
             }
+            if (image_due) issue_image();
             // On abort, let every copy this CTA issued land before it exits.
             if (*s_abort) {
+                if (FUSED && p.image) mbar_wait_bounded(sbase + kHdrImage, 0u);
                 const int issued = it;
                 for (int k = issued > S ? issued - S : 0; k < issued; ++k)
                     mbar_wait_bounded(full0 + 8 * (k % S), (uint32_t)(k / S) & 1u);
@@ -958,7 +1022,15 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         float* dxs = reinterpret_cast<float*>(qs + qbytes);
         int* bss = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
         int* hss = reinterpret_cast<int*>(qs + qbytes + 8u * (uint32_t)(M * nb));
-        const uint32_t qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk);
+        uint32_t qm = 0;
+        if (p.image) {
+            // the producer copies the image in; masks sit just below the activations
+            if (!mbar_wait_or_abort(sbase + kHdrImage, 0u, s_abort)) qm = 0;
+            const uint32_t* masks = reinterpret_cast<const uint32_t*>(smem + kGemvSmemHeader - kImageHeader);
+            for (int c = 0; c < p.image_ctas; ++c) qm |= masks[c];
+        } else {
+            qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk);
+        }
         quirk = (TYPE == kQ8_0 || TYPE == kQ6_K) ? qm : 0u;
         as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), smem_addr(hss), act_row_stride(p.K), nb};
     } else {
