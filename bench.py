@@ -24,7 +24,12 @@ The printed JSON line:
 
 --impl reference runs the reference's CPU implementation on the same sweep.
 --gpus N (under torchrun) runs N independent replicas, one per GPU: weak
-scaling, no collective on the data path.
+scaling, no collective on the data path; at N > 1 the line also carries
+`sharded_70b`, BASELINE config 5 on the same N GPUs.
+--workload 70b makes config 5 the bench line (any N, strong scaling): the
+Llama-3-70B decode sweep with every matrix row-sharded over the GPUs, the
+output of each projection all-gathered by the GEMV's own NVLink peer stores
+(cllm_inference_b200.sharded), with the NCCL all-gather path timed beside it.
 """
 from __future__ import annotations
 
