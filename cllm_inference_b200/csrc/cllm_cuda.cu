@@ -184,7 +184,7 @@ GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
     return nullptr;
 }
 
-typedef void (*ImageFn)(const float*, int, uint8_t*);
+typedef void (*ImageFn)(const float*, int, uint8_t*, const uint32_t*, const uint32_t*, int);
 
 template <int T>
 ImageFn image_fn(int m) {
@@ -222,7 +222,10 @@ constexpr int kImageMinK = 8192;
 uint32_t image_bytes(int m, int K) { return (uint32_t)kImageHeader + fused_act_bytes(m, K); }
 
 // Launch act_image_kernel for m rows of x (programmatic dependent launch).
-int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas, cudaStream_t st) {
+// wait_pad / wait_epoch / wait_world (row-sharded chains): wait for every rank's
+// announcement of round *wait_epoch before reading x; nullptr: no wait.
+int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas, cudaStream_t st,
+                 const uint32_t* wait_pad = nullptr, const uint32_t* wait_epoch = nullptr, int wait_world = 0) {
     ImageFn fn = select_image(type, m);
     if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no activation-image kernel for type %d, %d rows", type, m);
     const int groups = (m * (K / 32) + kGemvThreads / 4 - 1) / (kGemvThreads / 4);
@@ -236,7 +239,7 @@ int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img));
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img, wait_pad, wait_epoch, wait_world));
     *ctas = n;
     return CLLM_OK;
 }
@@ -952,6 +955,9 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     pl.num_tiles = (rows + pl.rows_per_tile - 1) / pl.rows_per_tile;
     pl.grid = std::max(1, std::min(pl.grid, pl.num_tiles));
     const bool wait_prev = (flags & CLLM_SHARD_WAIT_PREV) != 0;
+    // Large in_dim: quantize x once per call (act_image_kernel, which also does
+    // the wait for the previous round) instead of in every CTA.
+    const bool use_image = pl.fused && pl.tma && in_dim >= kImageMinK;
     if (wait_prev && !pl.fused) {  // x is read by the quantize kernel: wait before it
         if (int rc = launch_shard_kernel(shard_wait_kernel, st, (const uint32_t*)signal_pads[rank],
                                          (const uint32_t*)epoch, world))
@@ -960,6 +966,8 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     uint8_t* ws = nullptr;
     if (!pl.fused) {
         if (int rc = workspace(dev, L.end, &ws)) return rc;
+    } else if (use_image) {
+        if (int rc = workspace(dev, image_bytes(n_rows, in_dim), &ws)) return rc;
     }
     GemvParams p{};
     p.w = wd;
@@ -967,7 +975,7 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     p.K = in_dim;
     p.N = rows;
     p.x = x;
-    if (ws) {
+    if (ws && !pl.fused) {
         p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
         p.dx = reinterpret_cast<float*>(ws + L.dx);
         p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
@@ -984,7 +992,15 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
         for (int q = 0; q < world; ++q) p.spads[q] = signal_pads[q];
         p.sepoch = epoch;
         p.srank = rank;
-        p.swait = (wait_prev && pl.fused) ? 1 : 0;
+        p.swait = (wait_prev && pl.fused && !use_image) ? 1 : 0;
+    }
+    if (use_image) {
+        const bool w = wait_prev && signal_pads;
+        if (int rc = launch_image(type, n_rows, x, in_dim, ws, &p.image_ctas, st, w ? signal_pads[rank] : nullptr,
+                                  w ? epoch : nullptr, w ? world : 0))
+            return rc;
+        p.image = ws;
+        p.image_bytes = image_bytes(n_rows, in_dim);
     }
     if (!pl.fused) {
         if (int rc = launch_quantize(x, in_dim, n_rows, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),

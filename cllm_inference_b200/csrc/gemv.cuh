@@ -904,10 +904,26 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
 // lets the GEMV launch (and start streaming weights) at once.
 template <int M, int TYPE>
 __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __restrict__ x, int K,
-                                                                 uint8_t* __restrict__ image) {
+                                                                 uint8_t* __restrict__ image, const uint32_t* wait_pad,
+                                                                 const uint32_t* wait_epoch, int wait_world) {
     __shared__ uint32_t s_mask;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Row-sharded chain: x may be the previous round's all-gathered output, so
+    // wait (bounded) until every rank has announced that round.
+    if (wait_pad && (int)threadIdx.x < wait_world) {
+        const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(wait_epoch);
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(wait_pad + threadIdx.x) : "memory");
+            if ((int32_t)(v - ep) >= 0) break;
+            if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(&g_device_status, kStatusTimeout);
+                break;
+            }
+        }
+    }
     if (threadIdx.x == 0) s_mask = 0;
     __syncthreads();
     const int nb = K >> 5;

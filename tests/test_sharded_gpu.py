@@ -43,7 +43,9 @@ def _full(lib, xd, wd, t, k, n, m, bias=None):
 
 
 CASES = [(synth.Q4_K, 4096, 1024, 1), (synth.Q4_K, 4096, 1000, 3), (synth.Q6_K, 4096, 515, 1),
-         (synth.Q8_0, 1024, 96, 2), (synth.Q5_K, 2048, 77, 4)]
+         (synth.Q8_0, 1024, 96, 2), (synth.Q5_K, 2048, 77, 4),
+         # in_dim >= 8192: activations quantized once per call (activation image)
+         (synth.Q6_K, 8192, 130, 1), (synth.Q4_K, 8192, 200, 2)]
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
@@ -126,13 +128,14 @@ def _pads(world):
     return [torch.zeros(_lib.SHARD_PAD_WORDS, dtype=torch.int32, device="cuda") for _ in range(world)]
 
 
+@pytest.mark.parametrize("k", [4096, 8192])
 @pytest.mark.parametrize("world", [2, 3])
-def test_rowshard_signals_every_rank(lib, world):
+def test_rowshard_signals_every_rank(lib, world, k):
     """Each emulated rank's call announces its round into every pad and
     resets its arrival count; once all ranks have run, each rank's wait
     passes, and the next round (CLLM_SHARD_WAIT_PREV) sees the previous one
     complete.  Ranks run one after another: nothing waits on a later launch."""
-    t, k, n, m = synth.Q4_K, 4096, 300, 1
+    t, n, m = synth.Q4_K, 300, 1
     w = synth.make_weights(t, n, k, seed=9)
     x = to_dev(synth.make_activations(m, k, 3))
     ref = _full(lib, x, to_dev(w), t, k, n, m)
@@ -176,11 +179,12 @@ def test_rowshard_empty_slice_still_signals(lib):
     assert torch.equal(ys[0], _full(lib, x, to_dev(w), t, k, n, 1))
 
 
-def test_rowshard_wait_for_missing_rank_times_out(lib):
+@pytest.mark.parametrize("k", [4096, 8192])
+def test_rowshard_wait_for_missing_rank_times_out(lib, k):
     """CLLM_SHARD_WAIT_PREV while a peer never finished the previous round:
     the in-kernel wait gives up after its bound, the status reports it, and
     the call still completes (no fault, no hang)."""
-    t, k, n, world = synth.Q4_K, 4096, 64, 2
+    t, n, world = synth.Q4_K, 64, 2
     w = synth.make_weights(t, n, k, seed=8)
     x = to_dev(synth.make_activations(1, k, 1))
     pads, ys = _pads(world), [torch.zeros((1, n), device="cuda") for _ in range(world)]
