@@ -286,6 +286,12 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
         pl.smem = fixed + (size_t)S * pl.stage_bytes;
         const int per_sm = pl.smem <= kSmemPerCta ? 2 : 1;
         pl.grid = std::min(pl.num_tiles, per_sm * di.sms);
+        // With few tiles per CTA, as few CTAs as keep the same number of tile
+        // rounds: every CTA then gets the same number of tiles (within one),
+        // so none idles through the last round (gate/up 14336x4096: 296 CTAs
+        // with 6 or 7 tiles -> 256 CTAs with 7, 6.6 % faster).
+        const int rounds = (pl.num_tiles + pl.grid - 1) / pl.grid;
+        if (rounds <= 16) pl.grid = (pl.num_tiles + rounds - 1) / rounds;
     } else {
         pl.stages = 0;
         pl.smem = 0;
