@@ -392,9 +392,16 @@ def main():
             "gemv_tok_s": round(1e3 / ms_step, 2),
             "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(), "plan_q4k_gate": plan_q4k}
-    if dist is not None:
-        # BASELINE config 5 at this GPU count: the row-sharded 70B sweep
+    if not args.quick:
+        # BASELINE config 5 at this GPU count (a one-process group at N=1): the
+        # row-sharded 70B sweep, with its parity check
+        solo = dist is None
+        if solo:
+            dist = init_solo_group(torch, dev.index)
         line["sharded_70b"] = measure_70b(torch, dist, dev, world, rank, args.steps, args.warmup)
+        if solo:
+            dist.destroy_process_group()
+            dist = None
     line.update({k: v for k, v in extra.items() if k != "e2e"})
     if "e2e" in extra:
         line["e2e"] = extra["e2e"]
@@ -407,11 +414,25 @@ def main():
     return 0
 
 
+def init_solo_group(torch, local):
+    """A one-process NCCL group on a free local port (for the row-sharded path at N=1)."""
+    import datetime
+    import socket
+
+    import torch.distributed as dist
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist
+
+
 def run_70b(args):
     """--workload 70b: BASELINE config 5 as the bench line (any GPU count; a
     one-process group at N=1)."""
     import datetime
-    import socket
 
     import torch
     import torch.distributed as dist
@@ -421,11 +442,7 @@ def run_70b(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world == 1 and "MASTER_PORT" not in os.environ:
-        with socket.socket() as sk:
-            sk.bind(("127.0.0.1", 0))
-            port = sk.getsockname()[1]
-        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
-                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        init_solo_group(torch, local)
     else:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -442,7 +459,8 @@ def run_70b(args):
                        "calls_per_step": r["calls_per_step"], "bytes_per_step": r["bytes_per_step"],
                        "l2": "inputs larger than L2 (8 distinct layers = 4.3 GB, cycled)",
                        "parallelism": f"row-sharded over {world} GPU(s)"},
-            "tok_s": r["tok_s"], "pct_of_peak": round(100.0 * r["value"] / world / peak, 2),
+            "tok_s": r["tok_s"], "parity": r["parity"], "parity_detail": r["parity_detail"],
+            "pct_of_peak": round(100.0 * r["value"] / world / peak, 2),
             "peak_source": peak_kind, "first_8_layers_ms": r["first_8_layers_ms"], "gather": r["gather"],
             "clocks": clocks.summary()}
     dist.destroy_process_group()
@@ -551,13 +569,64 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
 
     _lib.check(_lib.load().cllm_cuda_check_device_status())
     del g, g8, g8n
+    parity = sharded_parity(torch, dist, grp, dev, world, rank)
     grp.close()
     return {"workload": "Llama-3-70B decode sweep (BASELINE config 5), M=1, row-sharded",
+            "parity": parity["ok"], "parity_detail": parity,
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "tok_s": round(1e3 / ms, 2), "bytes_per_step": step_bytes, "calls_per_step": len(calls),
             "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings); its last warp "
                                      "signals every rank; the next call waits for all signals",
             "first_8_layers_ms": {"fused_peer_stores": round(ms8, 4), "nccl_all_gather": round(ms8n, 4)}}
+
+
+def sharded_parity(torch, dist, grp, dev, world, rank):
+    """Correctness of the row-sharded path at this GPU count: one 70B layer
+    (and the lm_head) generated identically on every rank; every rank
+    compares the gathered y of each projection -- and of two chained pairs
+    (q -> o, gate -> down), where a call's input is the previous call's
+    gathered output -- with its own unsharded one-GPU matmul_quant of the full
+    matrix.  The sharded call sums every row exactly as the unsharded call, so
+    equality is bitwise; the verdict is the AND over ranks."""
+    from cllm_inference_b200 import _lib, sharded
+
+    lib = _lib.load()
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+
+    def full_call(x, wf, t, k, n):
+        y = torch.empty(n, dtype=torch.float32, device=dev)
+        _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(wf.data_ptr()), t,
+                                              None, k, n, 1, ctypes.c_void_p(y.data_ptr()), 0, st()))
+        return y
+
+    mats = {}
+    for (name, t, k, n) in LAYER_70B + [LM_HEAD_70B]:
+        wf = synth.make_weights_torch(t, n, k, seed=424242 + len(name) * 13 + n, device=dev)
+        mats[name] = (wf, grp.shard(wf, t, k, n), t, k, n)
+    xs = {k: torch.from_numpy(synth.make_activations(1, k, 77 + k)).to(dev) for k in (8192, 28672)}
+    bad, checked = [], 0
+    for name, (wf, sw, t, k, n) in mats.items():
+        y = grp.matmul(xs[k], sw, 1).reshape(-1)
+        ok = torch.equal(y, full_call(xs[k], wf, t, k, n))
+        checked += 1
+        if not ok:
+            bad.append(name)
+    for a, b in (("q", "o"), ("gate", "down")):
+        wa, swa, ta, ka, na = mats[a]
+        wb, swb, tb, kb, nb = mats[b]
+        ya = grp.matmul_unread(xs[ka], swa, 1, chain=True)
+        yb = grp.matmul(ya, swb, 1).reshape(-1)
+        ref = full_call(full_call(xs[ka], wa, ta, ka, na), wb, tb, kb, nb)
+        checked += 1
+        if not torch.equal(yb, ref):
+            bad.append(f"{a}->{b}")
+    torch.cuda.synchronize()
+    _lib.check(lib.cllm_cuda_check_device_status())
+    flag = torch.tensor([0 if bad else 1], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    del mats
+    return {"ok": bool(flag.item() == 1), "checks_per_rank": checked, "mismatch_on_rank0": bad if rank == 0 else None,
+            "rule": "gathered y == unsharded one-GPU matmul_quant, bitwise, on every rank"}
 
 
 def capture_graph(torch, fn):

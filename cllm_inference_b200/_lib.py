@@ -49,6 +49,7 @@ SIGNATURES = {
     "cllm_cuda_matmul_quant": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _U, _P]),
     "cllm_cuda_matmul_q8": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
     "cllm_cuda_row_partials": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
+    "cllm_cuda_matmul_partials": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "cllm_cuda_dequantize": (_I, [_P, _I, _I64, _P, _P]),
     "cllm_cuda_matmul_plan": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_I), _I]),
     "cllm_cuda_matmul_quant_noalloc": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _P]),

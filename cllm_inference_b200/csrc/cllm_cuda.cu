@@ -86,6 +86,7 @@ struct Workspace {
     size_t cap = 0;
 };
 Workspace g_ws[64];
+std::mutex g_ws_mu[64];  // one per device: held from workspace() until the call's kernels are enqueued
 
 struct WeightRange {
     size_t bytes;
@@ -120,9 +121,14 @@ int ensure_device(int* out_dev) {
     return CLLM_OK;
 }
 
-// Grow the device workspace to at least `bytes` (never shrinks).
-int workspace(int dev, size_t bytes, uint8_t** out) {
-    std::lock_guard<std::mutex> lk(g_mu);
+// Grow the device workspace to at least `bytes` (never shrinks).  Takes the
+// device's workspace lock into `lk`; the caller keeps it until every kernel
+// that uses the workspace is enqueued, so another host thread cannot grow
+// (free and reallocate) the buffer between this call and those launches.
+// What the lock cannot order is work already enqueued on other streams:
+// calls that may overlap on the GPU must be serialised by the caller.
+int workspace(int dev, size_t bytes, uint8_t** out, std::unique_lock<std::mutex>& lk) {
+    lk = std::unique_lock<std::mutex>(g_ws_mu[dev]);
     Workspace& ws = g_ws[dev];
     if (ws.cap < bytes) {
         if (ws.ptr) {
@@ -159,7 +165,14 @@ typedef void (*GemvFn)(GemvParams);
 
 template <int T>
 GemvFn gemv_fn(bool tma, bool fused, bool emit, int m) {
-    if (emit) return tma ? gemv_tma_kernel<T, 1, true, false> : gemv_direct_kernel<T, 1, true>;
+    // Parity builds (EMIT: partials instead of y) exist for 1 and 4 activation rows.
+    if (emit && m == 1)
+        return !tma ? gemv_direct_kernel<T, 1, true>
+                    : (fused ? gemv_tma_kernel<T, 1, true, true> : gemv_tma_kernel<T, 1, true, false>);
+    if (emit && m == 4)
+        return !tma ? gemv_direct_kernel<T, 4, true>
+                    : (fused ? gemv_tma_kernel<T, 4, true, true> : gemv_tma_kernel<T, 4, true, false>);
+    if (emit) return nullptr;
 #define CLLM_CASE(MM)                                                                     \
     case MM:                                                                              \
         return !tma ? gemv_direct_kernel<T, MM, false>                                    \
@@ -501,6 +514,52 @@ int noalloc_scratch(int dev, uint8_t** out) {
     return CLLM_OK;
 }
 
+
+// The decode-path launches of one call (device pointers): for every chunk of
+// up to 8 activation rows, the activation quantization its plan asks for
+// (fused into the GEMV; once per call into the activation image at img, when
+// img is given and the plan is fused; or the standalone quantize kernel into
+// the workspace at L) and the GEMV.  With partials != nullptr the same
+// kernels run in their parity build (EMIT), which writes the int32 block
+// partials [n_rows][out_dim][parts per row] instead of y, in chunks of 4 or
+// 1 rows.
+int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, const float* bd, int in_dim,
+               int out_dim, int n_rows, float* yd, int32_t* partials, uint8_t* ws, const ActLayout& L,
+               uint8_t* img, const DeviceInfo& di, cudaStream_t st) {
+    const bool emit = partials != nullptr;
+    const int64_t ppr = (type == kQ6_K ? 2 : 1) * (int64_t)(in_dim / 32);
+    for (int t0 = 0; t0 < n_rows;) {
+        const int left = n_rows - t0;
+        const int m = emit ? (left >= 4 ? 4 : 1) : std::min(8, left);
+        const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di, xd + (size_t)t0 * in_dim);
+        GemvParams p{};
+        p.w = wd;
+        p.row_bytes = row_bytes;
+        p.K = in_dim;
+        p.N = out_dim;
+        p.x = xd + (size_t)t0 * in_dim;
+        p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
+        p.dx = reinterpret_cast<float*>(ws + L.dx);
+        p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
+        p.fl = ws + L.fl;
+        p.bias = bd;
+        p.y = emit ? nullptr : yd + (size_t)t0 * out_dim;
+        p.partials = emit ? partials + (size_t)t0 * out_dim * ppr : nullptr;
+        fill_plan(p, pl);
+        if (!pl.fused) {
+            if (int rc = launch_quantize(p.x, in_dim, m, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
+                                         const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
+                return rc;
+        } else if (img && pl.tma) {
+            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st)) return rc;
+            p.image = img;
+            p.image_bytes = image_bytes(m, in_dim);
+        }
+        if (int rc = launch_gemv(type, emit, m, pl, p, st)) return rc;
+        t0 += m;
+    }
+    return CLLM_OK;
+}
 }  // namespace
 }  // namespace cllm
 
@@ -664,7 +723,8 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
     const bool want_image = !use_tc && in_dim >= kImageMinK;
     if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
     uint8_t* ws;
-    if (int rc = workspace(dev, total, &ws)) return rc;
+    std::unique_lock<std::mutex> ws_lock;
+    if (int rc = workspace(dev, total, &ws, ws_lock)) return rc;
 
     const float* xd = x;
     const float* bd = bias;
@@ -683,34 +743,10 @@ int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float*
         if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
             return rc;
     }
-    for (int t0 = 0; !use_tc && t0 < n_rows; t0 += 8) {
-        const int m = std::min(8, n_rows - t0);
-        const GemvPlan pl = plan_gemv(type, wd, row_bytes, in_dim, out_dim, m, true, di, xd + (size_t)t0 * in_dim);
-        GemvParams p{};
-        p.w = wd;
-        p.row_bytes = row_bytes;
-        p.K = in_dim;
-        p.N = out_dim;
-        p.x = xd + (size_t)t0 * in_dim;
-        p.qx = reinterpret_cast<int8_t*>(ws + L.qs);
-        p.dx = reinterpret_cast<float*>(ws + L.dx);
-        p.bs = reinterpret_cast<int32_t*>(ws + L.bs);
-        p.fl = ws + L.fl;
-        p.bias = bd;
-        p.y = yd + (size_t)t0 * out_dim;
-        p.partials = nullptr;
-        fill_plan(p, pl);
-        if (!pl.fused) {
-            if (int rc = launch_quantize(p.x, in_dim, m, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
-                                         const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
-                return rc;
-        } else if (want_image && pl.tma) {
-            uint8_t* img = ws + off_img;
-            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st)) return rc;
-            p.image = img;
-            p.image_bytes = image_bytes(m, in_dim);
-        }
-        if (int rc = launch_gemv(type, false, m, pl, p, st)) return rc;
+    if (!use_tc) {
+        if (int rc = run_decode(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, nullptr, ws, L,
+                                want_image ? ws + off_img : nullptr, di, st))
+            return rc;
     }
     if (flags & CLLM_Y_HOST) {
         CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
@@ -738,7 +774,8 @@ int cllm_cuda_matmul_q8(const float* scales, const int8_t* qs, const int32_t* bs
     const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
     const int64_t nb = in_dim / 32;
     uint8_t* ws;
-    if (int rc = workspace(dev, align256((size_t)n_rows * nb) + 256, &ws)) return rc;
+    std::unique_lock<std::mutex> ws_lock;
+    if (int rc = workspace(dev, align256((size_t)n_rows * nb) + 256, &ws, ws_lock)) return rc;
     const int64_t total = nb * n_rows;
     if (total > 0) {
         const int64_t grid = std::min<int64_t>((total + 7) / 8, 16LL * di.sms);
@@ -788,7 +825,8 @@ int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim
     // block; it is zero wherever no -128 activation meets a negative weight.
     const ActLayout L = act_layout(1, in_dim, 0);
     uint8_t* ws;
-    if (int rc = workspace(dev, L.end, &ws)) return rc;
+    std::unique_lock<std::mutex> ws_lock;
+    if (int rc = workspace(dev, L.end, &ws, ws_lock)) return rc;
     CLLM_CUDA_TRY(cudaMemsetAsync(ws + L.dx, 0, L.fl - L.dx, st));
     CLLM_CUDA_TRY(cudaMemsetAsync(ws + L.fl, 1, L.end - L.fl, st));
     for (int t = 0; t < n_rows; ++t) {
@@ -807,6 +845,31 @@ int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim
         if (int rc = launch_gemv(type, true, 1, pl, p, st)) return rc;
     }
     return CLLM_OK;
+}
+
+int cllm_cuda_matmul_partials(const float* x, const void* w, int type, int in_dim, int out_dim, int n_rows,
+                              int32_t* partials, void* stream) {
+    if (in_dim < 0 || out_dim < 0 || n_rows < 0) return fail(CLLM_ERR_INVALID_ARG, "matmul_partials: negative size");
+    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (in_dim % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "matmul_quant: in_dim not divisible by block size");
+    if (n_rows == 0 || out_dim == 0 || in_dim == 0) return CLLM_OK;
+    if (!x || !w || !partials) return fail(CLLM_ERR_INVALID_ARG, "matmul_partials: null pointer");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
+    const int mchunk = std::min(n_rows, 4);
+    const ActLayout L = act_layout(mchunk, in_dim, 0);
+    const bool want_image = in_dim >= kImageMinK;
+    size_t total = L.end;
+    const size_t off_img = total;
+    if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
+    uint8_t* ws;
+    std::unique_lock<std::mutex> ws_lock;
+    if (int rc = workspace(dev, total, &ws, ws_lock)) return rc;
+    return run_decode(type, static_cast<const uint8_t*>(w), row_bytes, x, nullptr, in_dim, out_dim, n_rows,
+                      nullptr, partials, ws, L, want_image ? ws + off_img : nullptr, g_dev[dev],
+                      static_cast<cudaStream_t>(stream));
 }
 
 int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream) {
@@ -970,10 +1033,11 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
             return rc;
     }
     uint8_t* ws = nullptr;
+    std::unique_lock<std::mutex> ws_lock;
     if (!pl.fused) {
-        if (int rc = workspace(dev, L.end, &ws)) return rc;
+        if (int rc = workspace(dev, L.end, &ws, ws_lock)) return rc;
     } else if (use_image) {
-        if (int rc = workspace(dev, image_bytes(n_rows, in_dim), &ws)) return rc;
+        if (int rc = workspace(dev, image_bytes(n_rows, in_dim), &ws, ws_lock)) return rc;
     }
     GemvParams p{};
     p.w = wd;

@@ -38,7 +38,7 @@ struct GemvParams {
     const uint8_t* fl;    // per-block "holds -128" flags [M][K/32]
     const float* bias;    // [N] or nullptr
     float* y;             // [M][N]
-    int32_t* partials;    // EMIT only: [N][parts per row] for activation row 0
+    int32_t* partials;    // EMIT only: [M][N][parts per row] int32 block partials (y is not written)
     int rows_per_tile;    // R
     int wpr;              // warps per row (R * wpr == warps per CTA)
     int num_tiles;
@@ -241,7 +241,7 @@ struct ActSmem {
 
 template <int TYPE, int M, bool EMIT, int ALIGN, class Src, class Act>
 __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u, const GemvParams& p,
-                                          float (&acc)[M], int32_t* prow, uint32_t quirk) {
+                                          float (&acc)[M], int32_t* prow, int64_t pstride, uint32_t quirk) {
     if constexpr (TYPE == kQ4_K) {
         const int s = u >> 2, q = u & 3;
         const uint32_t o = 144u * (uint32_t)s;
@@ -268,7 +268,7 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
                 P0 = dp4a(lo[i], xa[i], P0);
                 P1 = dp4a(hi[i], xb[i], P1);
             }
-            if constexpr (EMIT) { prow[b0] = P0; prow[b0 + 1] = P1; }
+            if constexpr (EMIT) { prow[t * pstride + b0] = P0; prow[t * pstride + b0 + 1] = P1; }
             const float2 dd = act.dx2(t, b0);
             const int2 ss = act.bs2(t, b0);
             acc[t] = fmaf(d1 * dd.x, i2f_exact(P0), acc[t]);
@@ -304,7 +304,7 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
                 P0 = dp4a(q0[i], xa[i], P0);
                 P1 = dp4a(q1[i], xb[i], P1);
             }
-            if constexpr (EMIT) { prow[b0] = P0; prow[b0 + 1] = P1; }
+            if constexpr (EMIT) { prow[t * pstride + b0] = P0; prow[t * pstride + b0 + 1] = P1; }
             const float2 dd = act.dx2(t, b0);
             const int2 ss = act.bs2(t, b0);
             acc[t] = fmaf(d1 * dd.x, i2f_exact(P0), acc[t]);
@@ -379,8 +379,9 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
                 }
             }
             if constexpr (EMIT) {
-                prow[2 * bA] = PA0; prow[2 * bA + 1] = PA1;
-                prow[2 * bB] = PB0; prow[2 * bB + 1] = PB1;
+                int32_t* pt = prow + t * pstride;
+                pt[2 * bA] = PA0; pt[2 * bA + 1] = PA1;
+                pt[2 * bB] = PB0; pt[2 * bB + 1] = PB1;
             }
             const float2 dxAB = act.dx_q6(t, bA);
             // sc*P products are exact integers below 2^24, as in the reference
@@ -404,7 +405,7 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
 #pragma unroll
                 for (int i = 0; i < 8; ++i) P += signtrick_fix((int)q[i], x[i]);
             }
-            if constexpr (EMIT) prow[b] = P;
+            if constexpr (EMIT) prow[t * pstride + b] = P;
             acc[t] = fmaf(d * act.dx1(t, b), i2f_exact(P), acc[t]);
         }
     } else if constexpr (TYPE == kQ4_0) {
@@ -426,7 +427,7 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
             int P = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) P = dp4a(hi[i], x[4 + i], dp4a(lo[i], x[i], P));
-            if constexpr (EMIT) prow[b] = P;
+            if constexpr (EMIT) prow[t * pstride + b] = P;
             acc[t] = fmaf(d * act.dx1(t, b), i2f_exact(P - 8 * act.bs1(t, b)), acc[t]);
         }
     } else if constexpr (TYPE == kQ5_0) {
@@ -449,7 +450,7 @@ __device__ __forceinline__ void gemv_unit(const Src& src, const Act& act, int u,
             int P = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) P = dp4a(hi[i], x[4 + i], dp4a(lo[i], x[i], P));
-            if constexpr (EMIT) prow[b] = P;
+            if constexpr (EMIT) prow[t * pstride + b] = P;
             acc[t] = fmaf(d * act.dx1(t, b), i2f_exact(P - 16 * act.bs1(t, b)), acc[t]);
         }
     }
@@ -484,9 +485,11 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 
 // Q4_K row slice, activations and weights in shared memory (quant.cpp:549-590).
 // Lane unit u = 4s + q: sub-blocks 2q, 2q+1 of super-block s.
-template <int M>
+// EMIT (parity builds): also store each block's int32 partial at
+// prow[t * pstride + block].
+template <int M, bool EMIT>
 __device__ __forceinline__ void q4k_row_fused(uint32_t wrow, const ActSmem<kQ4_K>& act, int upr, int slice,
-                                              int wpr, float (&acc)[M]) {
+                                              int wpr, float (&acc)[M], int32_t* prow, int64_t pstride) {
     const int lane = threadIdx.x & 31;
     const int u0 = slice * 32 + lane;
     const int ustep = 32 * wpr;
@@ -536,6 +539,10 @@ __device__ __forceinline__ void q4k_row_fused(uint32_t wrow, const ActSmem<kQ4_K
             H1 = dp4a_us(hi[4], (int)x3.x, H1); H1 = dp4a_us(hi[5], (int)x3.y, H1);
             H1 = dp4a_us(hi[6], (int)x3.z, H1); H1 = dp4a_us(hi[7], (int)x3.w, H1);
             const int P1 = H1 >> 4;  // exact: every term is a multiple of 16
+            if constexpr (EMIT) {
+                prow[t * pstride + 2 * u] = P0;
+                prow[t * pstride + 2 * u + 1] = P1;
+            }
             const uint32_t sa = (uint32_t)(t * act.nb) * 4u + so;
             const uint2 dd = lds64(act.dx + sa), ss = lds64(act.bs + sa);
             const float dx0 = __uint_as_float(dd.x), dx1 = __uint_as_float(dd.y);
@@ -566,9 +573,11 @@ __device__ __forceinline__ void lds_field8(uint32_t a, bool odd, uint32_t (&w)[8
 }
 
 // Q6_K row slice, activations and weights in shared memory (quant.cpp:630-687).
-template <int M>
+// EMIT: also store the int32 half-block partials at prow[t * pstride + 2*block + half].
+template <int M, bool EMIT>
 __device__ __forceinline__ void q6k_row_fused(uint32_t wrow, const ActSmem<kQ6_K>& act, int upr, int slice,
-                                              int wpr, uint32_t quirk, float (&acc)[M]) {
+                                              int wpr, uint32_t quirk, float (&acc)[M], int32_t* prow,
+                                              int64_t pstride) {
     const int lane = threadIdx.x & 31;
     const int v0 = slice * 32 + lane;
     const int vstep = 32 * wpr;
@@ -637,6 +646,12 @@ __device__ __forceinline__ void q6k_row_fused(uint32_t wrow, const ActSmem<kQ6_K
                     PB1 += signtrick_fix(q6_to_s8(vb[i + 4]), xb[i + 4]);
                 }
             }
+            if constexpr (EMIT) {
+                const int bA = 8 * sb + 4 * g + pr, bB = bA + 2;
+                int32_t* pt = prow + t * pstride;
+                pt[2 * bA] = PA0; pt[2 * bA + 1] = PA1;
+                pt[2 * bB] = PB0; pt[2 * bB + 1] = PB1;
+            }
             const uint2 dd = lds64(act.dx + 4u * (uint32_t)(t * act.nb + 2 * v));
             // sc*P sums are exact integers (|.| <= 2^24), as the reference's float sums
             const float inA = (float)(sA0 * PA0 + sA1 * PA1), inB = (float)(sB0 * PB0 + sB1 * PB1);
@@ -695,14 +710,16 @@ __device__ __forceinline__ void gemv_row_slice(const Src& src, const Act& act, i
     const int lane = threadIdx.x & 31;
     const int upr = units_per_row(TYPE, p.K);
     int32_t* prow = nullptr;
+    int64_t pstride = 0;
     if constexpr (EMIT) {
         const int ppr = (TYPE == kQ6_K) ? 2 * (p.K >> 5) : (p.K >> 5);
         prow = p.partials + (int64_t)row * ppr;
+        pstride = (int64_t)p.N * ppr;
     }
 #pragma unroll
     for (int t = 0; t < M; ++t) acc[t] = 0.0f;
     for (int u = slice * 32 + lane; u < upr; u += 32 * p.wpr)
-        gemv_unit<TYPE, M, EMIT, ALIGN>(src, act, u, p, acc, prow, quirk);
+        gemv_unit<TYPE, M, EMIT, ALIGN>(src, act, u, p, acc, prow, pstride, quirk);
     warp_sum<M>(acc);
 }
 
@@ -1063,10 +1080,18 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         if (r < rows) {
             float acc[M];
             SmemSrc src{ring + stg * p.stage_bytes + (uint32_t)(r * p.row_bytes)};
+            int32_t* prow = nullptr;
+            int64_t pstride = 0;
+            if constexpr (EMIT) {
+                const int ppr = (TYPE == kQ6_K) ? 2 * nb : nb;
+                prow = p.partials + (int64_t)(row0 + r) * ppr;
+                pstride = (int64_t)p.N * ppr;
+            }
             if constexpr (FUSED && TYPE == kQ4_K)
-                q4k_row_fused<M>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, acc);
+                q4k_row_fused<M, EMIT>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, acc, prow, pstride);
             else if constexpr (FUSED && TYPE == kQ6_K)
-                q6k_row_fused<M>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, quirk, acc);
+                q6k_row_fused<M, EMIT>(src.base, as, units_per_row(TYPE, p.K), slice, p.wpr, quirk, acc, prow,
+                                       pstride);
             else if constexpr (FUSED) gemv_row_slice<TYPE, M, EMIT, 16>(src, as, row0 + r, p, slice, quirk, acc);
             else gemv_row_slice<TYPE, M, EMIT, 16>(src, ag, row0 + r, p, slice, quirk, acc);
             if constexpr (!EMIT) {

@@ -95,8 +95,13 @@ int cllm_cuda_quantize_q8_0(const float* x, int64_t n, int rows, float* scales, 
  * (quant.cpp:1436).  Error strings follow quant.cpp:1379/1443/1370.
  * By default all pointers are device pointers and the call is asynchronous on
  * `stream`; the flags above switch x/bias, y and w to host memory.  Scratch
- * for the quantized activations comes from a per-device workspace that the
- * library grows on demand (cudaMalloc) and keeps until exit. */
+ * for the quantized activations comes from one workspace per device that the
+ * library grows on demand (cudaDeviceSynchronize, cudaFree, cudaMalloc) and
+ * keeps until exit; make a first call of the largest size before capturing
+ * calls into a CUDA graph.  Host threads may call concurrently (a per-device
+ * lock is held until the call's kernels are enqueued), but calls whose GPU
+ * work can overlap -- on different streams of one device -- share that
+ * workspace and race on it: order them (one stream, or events). */
 int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float* bias, int in_dim,
                            int out_dim, int n_rows, float* y, unsigned flags, void* stream);
 
@@ -118,6 +123,18 @@ int cllm_cuda_matmul_q8(const float* scales, const int8_t* qs, const int32_t* bs
  * the float sum); the values are those its AVX2 kernels form internally. */
 int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim, int out_dim,
                            int n_rows, int32_t* partials, void* stream);
+
+/* Parity entry for the production kernels: runs the launch plan that
+ * cllm_cuda_matmul_quant(x, w, ...) runs with device pointers and no bias --
+ * the same activation quantization (fused into the GEMV, or once per call for
+ * in_dim >= 8192) and the same dot loops -- in a build whose kernels store
+ * the exact int32 partials instead of y, in the layout of
+ * cllm_cuda_row_partials for n_rows activation rows of x (fp32, device).
+ * Rows are taken 4 or 1 at a time (both row counts of the production
+ * templates' loops).  No counterpart in the reference; the values are those
+ * its AVX2 kernels form internally (quant.cpp:549-687). */
+int cllm_cuda_matmul_partials(const float* x, const void* w, int type, int in_dim, int out_dim, int n_rows,
+                              int32_t* partials, void* stream);
 
 /* quant.cpp:371-389 (dequantize_block) for the six hot-path types: n values
  * from the blocks at src (device) into dst (device fp32).  Used by the
@@ -148,8 +165,11 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
  * process exits), so the call is limited to n_rows <= CLLM_NOALLOC_MAX_ROWS
  * and in_dim <= CLLM_NOALLOC_MAX_IN_DIM; larger calls fail with
  * CLLM_ERR_TOO_LARGE before any device work.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) and caches it:
- * make that first call before any stream capture.  All calls share the one
+ * looks up the array's device address (cudaGetSymbolAddress) and caches it
+ * per device index: make that first call before any stream capture.  The
+ * cached address does not survive cudaDeviceReset (or anything else that
+ * recreates the device's primary context): do not call this entry point on
+ * that device afterwards.  All calls share the one
  * array and every call rewrites the part it reads, so nothing needs clearing
  * between calls, but calls that can overlap on the GPU (other streams,
  * other host threads) race on it: serialise them. */

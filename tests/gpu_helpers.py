@@ -77,6 +77,36 @@ def partials(lib, qs: np.ndarray, w: np.ndarray, t: int, k: int, n: int, misalig
     return out.cpu().numpy()
 
 
+def matmul_partials(lib, x: np.ndarray, w: np.ndarray, t: int, k: int, n: int):
+    """Partials of the production kernels (cllm_cuda_matmul_partials): the
+    launch plan of matmul_quant on fp32 x, int32 partials instead of y."""
+    m = x.shape[0]
+    ppr = (2 if t == 14 else 1) * (k // 32)
+    xd = to_dev(x.astype(np.float32))
+    _, wp = dev_bytes(w)
+    out = torch.full((m, n, ppr), -7777777, dtype=torch.int32, device="cuda")
+    _lib.check(lib.cllm_cuda_matmul_partials(dptr(xd), wp, t, k, n, m, dptr(out), stream()))
+    torch.cuda.synchronize()
+    _lib.check(lib.cllm_cuda_check_device_status())
+    return out.cpu().numpy()
+
+
+def sample_rows(n: int, limit: int, seed: int = 0) -> np.ndarray:
+    """All rows when n <= limit, else the first and last 8 rows plus a seeded
+    sample (sorted, distinct)."""
+    if n <= limit:
+        return np.arange(n)
+    rng = np.random.default_rng(seed)
+    mid = rng.choice(np.arange(8, n - 8), size=limit - 16, replace=False)
+    return np.unique(np.concatenate([np.arange(8), mid, np.arange(n - 8, n)]))
+
+
+def row_subset(w: np.ndarray, rb: int, rows: np.ndarray) -> np.ndarray:
+    """The weight bytes of the given rows, back to back."""
+    w2 = np.ascontiguousarray(w).view(np.uint8).reshape(-1, rb)
+    return np.ascontiguousarray(w2[rows]).reshape(-1)
+
+
 def assert_rows_close(y_gpu, y_ref, abs_terms, rel=1e-5, what=""):
     """The north-star row tolerance: |y_gpu - y_ref| <= rel * sum|partial*scale|.
 

@@ -226,3 +226,35 @@ def test_plan_uses_tma_ring_and_fused_quantization(cuda, lib):
             assert info[1] == 1, (name, m, list(info))
             if not (m == 4 and k == 14336):
                 assert info[2] == 1 and info[0] == 1, (name, m, list(info))
+
+
+# The production loops (fused quantization; q4k_row_fused / q6k_row_fused for
+# Q4_K and Q6_K; the activation image for in_dim >= 8192) must form exactly the
+# reference's integer partials: checked through the parity build of the same
+# launch plan (cllm_cuda_matmul_partials) on the BASELINE config-2 and 70B shapes.
+@pytest.mark.parametrize("name,t,k,n", LAYER_SHAPES + LAYER_SHAPES_70B,
+                         ids=[s[0] for s in LAYER_SHAPES + LAYER_SHAPES_70B])
+@pytest.mark.parametrize("m", [1, 4])
+def test_production_partials_bit_exact(cuda, lib, oracle, name, t, k, n, m):
+    w = synth.make_weights(t, n, k, seed=n + 3 * k + t)
+    x = synth.make_activations(m, k, seed=k + m)
+    if m == 4:
+        x[2, 33] = np.nan  # a -128 activation: the sign-trick correction path
+    P = G.matmul_partials(lib, x, w, t, k, n)
+    rows = G.sample_rows(n, 1024, seed=n)
+    _, qs, _ = oracle.quantize(x)
+    Po = oracle.partials(G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows), qs)
+    assert np.array_equal(P[:, rows], Po), (name, m, int(np.sum(P[:, rows] != Po)))
+
+
+def test_production_partials_small_and_unaligned(cuda, lib, oracle):
+    """Every hot type on the direct-load and TMA paths, ragged row counts."""
+    for t in HOT_TYPES:
+        for k, n, m in ((256, 37, 1), (512, 70, 4), (4096, 129, 1)):
+            if k % synth.BLOCK[t]:
+                continue
+            w = synth.make_weights(t, n, k, seed=k + n + t)
+            x = synth.make_activations(m, k, seed=n)
+            _, qs, _ = oracle.quantize(x)
+            P = G.matmul_partials(lib, x, w, t, k, n)
+            assert np.array_equal(P, oracle.partials(w, t, k, n, qs)), (TYPE_NAMES[t], k, n, m)

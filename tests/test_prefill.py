@@ -48,3 +48,33 @@ def test_prefill_matches_decode_rows(cuda, lib):
     for r in range(8):
         y1 = G.matmul(lib, x[r:r + 1], w, t, k, n)
         G.assert_rows_close(y[r:r + 1], y1, ab[r:r + 1], 2 * REL_TOL, f"row {r}")
+
+
+def _tile_samples(count: int, tile: int, rng) -> np.ndarray:
+    """Indices covering every tile of `tile` entries: its first and last entry
+    and one seeded entry inside it."""
+    out = []
+    for b in range(0, count, tile):
+        e = min(count, b + tile) - 1
+        out += [b, e, int(rng.integers(b, e + 1))]
+    return np.unique(np.array(out))
+
+
+@pytest.mark.parametrize("m", [64, 512, 2048])
+def test_prefill_config3_exact_shape(cuda, lib, oracle, m):
+    """BASELINE config 3 itself: Q4_K 14336x4096 at M = 64, 512, 2048 on the
+    tcgen05 GEMM.  Every output row tile and every token tile is checked
+    against the oracle (three rows per 128-row tile; all tokens up to M=512,
+    three per 128-token tile at M=2048)."""
+    t, k, n = synth.Q4_K, 4096, 14336
+    w = synth.make_weights(t, n, k, seed=31337)
+    x = synth.make_activations(m, k, seed=m + 1)
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2, "expected the tcgen05 path"
+    y = G.matmul(lib, x, w, t, k, n)
+    rng = np.random.default_rng(m)
+    rows = _tile_samples(n, 128, rng)
+    toks = np.arange(m) if m <= 512 else _tile_samples(m, 128, rng)
+    yo, ab = oracle.matmul(x[toks], G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows),
+                           with_abs=True)
+    G.assert_rows_close(y[np.ix_(toks, rows)], yo, ab, REL_TOL, f"config 3 M={m}")

@@ -55,6 +55,29 @@ def test_noalloc_matches_regular_entry_on_two_calls(cuda, lib, oracle):
         G.assert_rows_close(y_na, y_ref, abs_terms, REL_TOL, f"noalloc {synth.NAMES[t]} m={m}")
 
 
+# Every loader and unit code the entry point can reach, and the exact-fit
+# limit: 8 rows x 32768 values fill the scratch array to its last byte.
+EDGE_CASES = [
+    (synth.Q4_K, MAX_IN_DIM, 300, MAX_ROWS),  # the limit case
+    (synth.Q6_K, 8192, 257, 2),               # in_dim >= 8192
+    (synth.Q6_K, 256, 45, 3),                 # 210-byte rows: the direct-load kernel
+    (synth.Q8_0, 1024, 70, 5),                # 32-value block types
+    (synth.Q5_0, 512, 33, 1),
+]
+
+
+@pytest.mark.parametrize("t,k,n,m", EDGE_CASES, ids=lambda c: str(c))
+def test_noalloc_edge_cases_against_oracle(cuda, lib, oracle, t, k, n, m):
+    w = synth.make_weights(t, n, k, seed=k + n)
+    x = synth.make_activations(m, k, seed=m + n)
+    bias = np.linspace(-1, 1, n, dtype=np.float32)
+    y_o, abs_terms = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+    for call in range(2):  # twice: the second call starts from the first one's scratch contents
+        y_ref, y_na = _both(lib, x, w, t, k, n, bias)
+        G.assert_rows_close(y_na, y_o, abs_terms, REL_TOL, f"noalloc vs oracle {synth.NAMES[t]} call {call}")
+        G.assert_rows_close(y_na, y_ref, abs_terms, 2 * REL_TOL, f"noalloc vs regular {synth.NAMES[t]}")
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda, lib):
     dummy = ctypes.c_void_p(256)
     rc = lib.cllm_cuda_matmul_quant_noalloc(dummy, dummy, synth.Q4_K, None, 4096, 16, MAX_ROWS + 1, dummy, None)
