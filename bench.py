@@ -402,6 +402,8 @@ def main():
         if solo:
             dist.destroy_process_group()
             dist = None
+    if not args.quick and rank == 0 and world == 1:
+        line["decode_8b"] = measure_engine(torch)
     line.update({k: v for k, v in extra.items() if k != "e2e"})
     if "e2e" in extra:
         line["e2e"] = extra["e2e"]
@@ -578,6 +580,128 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
             "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings); its last warp "
                                      "signals every rank; the next call waits for all signals",
             "first_8_layers_ms": {"fused_peer_stores": round(ms8, 4), "nccl_all_gather": round(ms8n, 4)}}
+
+
+def engine_bytes_per_step(path, ctx_pos_avg):
+    """Bytes one decode step of the engine must move: every linear weight
+    (each layer's 7 matrices + the output matrix), the embedding row, and the
+    fp32 K and V rows of all cached positions (avg over the timed steps)."""
+    from cllm_inference_b200 import gguf
+
+    meta, infos, _ = gguf.read_header(path)
+    total = 0
+    n_embd = meta["llama.embedding_length"]
+    for (name, t, dims, off) in infos:
+        if len(dims) != 2:
+            continue
+        cols, rows = dims
+        if name == "token_embd.weight":
+            total += gguf.tensor_bytes(t, 1, cols)
+        else:
+            total += gguf.tensor_bytes(t, rows, cols)
+    kv_dim = meta["llama.attention.head_count_kv"] * (n_embd // meta["llama.attention.head_count"])
+    total += 2 * 4 * kv_dim * ctx_pos_avg * meta["llama.block_count"]
+    return total
+
+
+def measure_engine(torch, cfg_name="8b", n_prompt=512, steps=256, ctx=2048, cpu_steps=4):
+    """the device-resident engine on a synthetic Llama-3-8B
+    GGUF file (Q4_K_M-style mix): a 512-token prefill, then 256 greedy decode
+    steps (the CUDA-graph step, argmax on the device), KV cache of 2048 fp32
+    positions.  Timed with CUDA events on the engine's stream.  The reference
+    engine (oracle/_ref) decodes a few tokens of the same file on the host
+    cores for the CPU figure."""
+    import shutil
+    import tempfile
+
+    from cllm_inference_b200 import gguf
+    from cllm_inference_b200.engine import Engine
+
+    shape = gguf.LLAMA3_8B
+    need = sum(gguf.tensor_bytes(t, r, c) for (_, t, r, c) in gguf.tensor_plan(shape)) + (64 << 20)
+    tmp_root = None
+    for cand in ("/dev/shm", tempfile.gettempdir()):
+        try:
+            if shutil.disk_usage(cand).free > need + (2 << 30):
+                tmp_root = cand
+                break
+        except OSError:
+            continue
+    if tmp_root is None:
+        return {"unavailable": f"no temporary file system with {need / 1e9:.1f} GB free for the model file"}
+    d = tempfile.mkdtemp(dir=tmp_root)
+    path = os.path.join(d, "llama3_8b_synthetic.gguf")
+    try:
+        t0 = time.perf_counter()
+        gguf.write_llama(path, shape, seed=8)
+        t_write = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        eng = Engine(path, ctx_limit=ctx)
+        t_load = time.perf_counter() - t0
+        st = torch.cuda.ExternalStream(eng.stream())
+        prompt = [int(v) for v in np.random.default_rng(4).integers(3, shape.vocab, n_prompt)]
+
+        def timed(fn):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            out = fn()
+            b.record(st)
+            b.synchronize()
+            return a.elapsed_time(b), out
+
+        # warm-up: a short prefill + decode, then the timed runs from an empty cache
+        eng.generate(prompt[:80], 8)
+        eng.reset()
+        ms_pre, _ = timed(lambda: eng.prefill(prompt, logits=False))
+        # generate() on the cached prompt re-runs only its last token (forward), then
+        # steps - 1 graph replays: `steps` decode steps in all
+        ms_dec, (toks, margins) = timed(lambda: eng.generate(prompt, steps))
+        launches = eng.launches_per_step
+        eng.close()
+        peak, peak_kind = measured_peaks()
+        bps = engine_bytes_per_step(path, n_prompt + steps // 2)
+        achieved = bps * steps / (ms_dec * 1e-3) / 1e9
+        out = {"workload": "Llama-3-8B-shaped synthetic GGUF (BASELINE config 4): 512-token prefill, then 256 "
+                           "greedy decode steps, fp32 KV cache of 2048 positions",
+               "decode_tok_s": round(steps / (ms_dec * 1e-3), 2), "decode_ms_per_token": round(ms_dec / steps, 4),
+               "prefill_tok_s": round(n_prompt / (ms_pre * 1e-3), 1), "prefill_ms": round(ms_pre, 3),
+               "roofline_decode": {"bound": "hbm", "bytes_per_step": int(bps), "achieved": round(achieved, 1),
+                                   "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                                   "peak_source": peak_kind,
+                                   "bytes": "all linear weights + embedding row + fp32 K/V of the cached "
+                                            "positions (mean context of the timed steps)"},
+               "kernel_launches_per_decode_step": launches, "model_write_s": round(t_write, 1),
+               "load_s": round(t_load, 1), "distinct_tokens": int(len(set(toks.tolist())))}
+        out["cpu_baseline"] = reference_engine_sample(path, cpu_steps)
+        return out
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
+def reference_engine_sample(path, steps):
+    """The reference's TransformerEngine (oracle/_ref) on the same file: a
+    16-token prefill, then `steps` forward calls, on all host cores."""
+    from oracle.oracle import ReferenceEngine, reference_engine_available
+
+    if not reference_engine_available():
+        return None
+    n_threads = os.cpu_count() or 1
+    eng = ReferenceEngine(path, n_threads=n_threads, ctx_limit=2048)
+    prompt = list(range(3, 19))
+    t0 = time.perf_counter()
+    eng.prefill(prompt)
+    t_pre = time.perf_counter() - t0
+    tok = 5
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lg = eng.forward(tok)
+        tok = int(np.argmax(lg))
+    dt = time.perf_counter() - t0
+    eng.close()
+    return {"value": round(steps / dt, 3), "unit": "tok/s (decode)", "cores": n_threads, "kind": "reference",
+            "prefill_tok_s": round(len(prompt) / t_pre, 2),
+            "sample": f"reference TransformerEngine (g++ -O3, AVX2): 16-token prefill, then {steps} forward calls "
+                      f"at context 17-{16 + steps}, ThreadPool({n_threads})"}
 
 
 def sharded_parity(torch, dist, grp, dev, world, rank):

@@ -51,6 +51,7 @@ SIGNATURES = {
     "cllm_cuda_row_partials": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "cllm_cuda_matmul_partials": (_I, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "cllm_cuda_dequantize": (_I, [_P, _I, _I64, _P, _P]),
+    "cllm_cuda_dequantize_f16": (_I, [_P, _I, _I64, _P, _P]),
     "cllm_cuda_matmul_plan": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_I), _I]),
     "cllm_cuda_matmul_quant_noalloc": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _P]),
     "cllm_cuda_shard_rows": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
@@ -58,6 +59,15 @@ SIGNATURES = {
                                              ctypes.POINTER(_P), _P, _U, _P]),
     "cllm_cuda_shard_wait": (_I, [_P, _P, _I, _P]),
     "cllm_cuda_shard_barrier": (_I, [ctypes.POINTER(_P), _P, _I, _I, _P]),
+    "cllm_cuda_engine_create": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
+    "cllm_cuda_engine_destroy": (_I, [_P]),
+    "cllm_cuda_engine_config": (_I, [_P, ctypes.POINTER(ctypes.c_int), _I]),
+    "cllm_cuda_engine_forward": (_I, [_P, _I, _P, ctypes.POINTER(ctypes.c_int)]),
+    "cllm_cuda_engine_prefill": (_I, [_P, _P, _I, _P, ctypes.POINTER(ctypes.c_int)]),
+    "cllm_cuda_engine_generate": (_I, [_P, _P, _I, _I, _P, _P]),
+    "cllm_cuda_engine_reset": (_I, [_P]),
+    "cllm_cuda_engine_seq_len": (_I, [_P]),
+    "cllm_cuda_engine_stream": (_I, [_P, ctypes.POINTER(_P)]),
     "cllm_cuda_check_device_status": (_I, []),
     "cllm_cuda_last_error": (_I, [ctypes.c_char_p, _SZ]),
 }

@@ -22,6 +22,7 @@
 #include "../../include/cllm_cuda.h"
 #include "common.cuh"
 #include "dequant.cuh"
+#include "fallback.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "shard.cuh"
@@ -468,6 +469,25 @@ int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const fl
     return CLLM_OK;
 }
 
+// matmul_quant for a type without an integer dot kernel (quant.cpp:1404-1430):
+// the dequantize-and-float-dot kernel, 8 activation rows per launch.
+int launch_fallback(int type, const uint8_t* w, int64_t row_bytes, const float* x, const float* bias, int K, int N,
+                    int n_rows, float* y, cudaStream_t st) {
+    typedef void (*Fn)(const uint8_t*, int, int64_t, int, int, const float*, const float*, float*);
+    static const Fn fns[8] = {gemv_fallback_kernel<1>, gemv_fallback_kernel<2>, gemv_fallback_kernel<3>,
+                              gemv_fallback_kernel<4>, gemv_fallback_kernel<5>, gemv_fallback_kernel<6>,
+                              gemv_fallback_kernel<7>, gemv_fallback_kernel<8>};
+    const int rows_per_cta = kFallbackWarps * 32;
+    const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
+    for (int t0 = 0; t0 < n_rows && grid > 0; t0 += 8) {
+        const int m = std::min(8, n_rows - t0);
+        fns[m - 1]<<<grid, rows_per_cta, 0, st>>>(w, type, row_bytes, K, N, x + (size_t)t0 * K, bias,
+                                                  y + (size_t)t0 * N);
+        CLLM_CUDA_TRY(cudaGetLastError());
+    }
+    return CLLM_OK;
+}
+
 // Layout of the quantized activations inside the workspace.
 struct ActLayout {
     size_t qs, dx, bs, fl, end;
@@ -560,6 +580,105 @@ int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, 
     }
     return CLLM_OK;
 }
+// matmul_quant / matmul_quant_batch (quant.cpp:1374-1475) behind
+// cllm_cuda_matmul_quant.  Scratch: the device workspace (scratch == nullptr),
+// or a caller-owned buffer of scratch_cap bytes (the engine's decode step,
+// whose captured graph must keep pointing at memory that never moves).  With
+// need != nullptr only the scratch size is computed (*need) and nothing runs.
+int matmul_quant_impl(const float* x, const void* w, int type, const float* bias, int in_dim, int out_dim,
+                      int n_rows, float* y, unsigned flags, cudaStream_t st, uint8_t* scratch, size_t scratch_cap,
+                      size_t* need) {
+    const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
+    if (n_rows <= 0) return CLLM_OK;  // quant.cpp:1436
+    if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))
+        return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
+    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
+    const int bsz = block_size_of(type);
+    if (in_dim % bsz != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
+    const bool fallback = !has_vec_dot_of(type);
+    if (fallback && !dequant_supported(type))
+        return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
+    if (out_dim == 0) return CLLM_OK;
+    if (!need && (!y || (in_dim > 0 && (!x || !w)))) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const DeviceInfo& di = g_dev[dev];
+
+    const int64_t row_bytes = (int64_t)(in_dim / bsz) * type_size_of(type);
+    const uint8_t* wd = static_cast<const uint8_t*>(w);
+    if (flags & CLLM_W_HOST) {
+        size_t avail = 0;
+        if (lookup(w, &wd, &avail) != CLLM_OK)
+            return fail(CLLM_ERR_NOT_REGISTERED, "%s: weight pointer %p is not inside a registered range",
+                        fname, w);
+        if ((uint64_t)row_bytes * (uint64_t)out_dim > avail)
+            return fail(CLLM_ERR_INVALID_ARG, "%s: weight matrix runs past its registered range", fname);
+    }
+
+    const bool use_tc = !fallback && prefill_eligible(type, wd, row_bytes, in_dim, n_rows);
+    const int mchunk = std::min(n_rows, 8);
+    const ActLayout L = act_layout(use_tc || fallback ? 0 : mchunk, in_dim, 0);
+    size_t off_x = L.end, off_b = L.end, off_y = L.end, total = L.end;
+    if (flags & CLLM_X_HOST) {
+        off_x = total;
+        total = align256(total + (size_t)n_rows * in_dim * 4);
+        off_b = total;
+        if (bias) total = align256(total + (size_t)out_dim * 4);
+    }
+    if (flags & CLLM_Y_HOST) {
+        off_y = total;
+        total = align256(total + (size_t)n_rows * out_dim * 4);
+    }
+    const size_t off_pre = total;
+    if (use_tc) total += prefill_bytes(n_rows, in_dim);
+    const size_t off_img = total;
+    const bool want_image = !use_tc && !fallback && in_dim >= kImageMinK;
+    if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
+    if (need) {
+        *need = total;
+        return CLLM_OK;
+    }
+    uint8_t* ws = scratch;
+    std::unique_lock<std::mutex> ws_lock;
+    if (scratch) {
+        if (total > scratch_cap)
+            return fail(CLLM_ERR_TOO_LARGE, "%s: %zu bytes of scratch needed, %zu given", fname, total, scratch_cap);
+    } else if (int rc = workspace(dev, total, &ws, ws_lock)) {
+        return rc;
+    }
+
+    const float* xd = x;
+    const float* bd = bias;
+    float* yd = y;
+    if (flags & CLLM_X_HOST) {
+        xd = reinterpret_cast<float*>(ws + off_x);
+        CLLM_CUDA_TRY(cudaMemcpyAsync((void*)xd, x, (size_t)n_rows * in_dim * 4, cudaMemcpyHostToDevice, st));
+        if (bias) {
+            bd = reinterpret_cast<float*>(ws + off_b);
+            CLLM_CUDA_TRY(cudaMemcpyAsync((void*)bd, bias, (size_t)out_dim * 4, cudaMemcpyHostToDevice, st));
+        }
+    }
+    if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
+
+    if (use_tc) {
+        if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
+            return rc;
+    }
+    if (fallback) {
+        if (int rc = launch_fallback(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, st)) return rc;
+    } else if (!use_tc) {
+        if (int rc = run_decode(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, nullptr, ws, L,
+                                want_image ? ws + off_img : nullptr, di, st))
+            return rc;
+    }
+    if (flags & CLLM_Y_HOST) {
+        CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
+        CLLM_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return CLLM_OK;
+}
+
 }  // namespace
 }  // namespace cllm
 
@@ -675,84 +794,8 @@ int cllm_cuda_quantize_q8_0(const float* x, int64_t n, int rows, float* scales, 
 
 int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float* bias, int in_dim,
                            int out_dim, int n_rows, float* y, unsigned flags, void* stream) {
-    const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
-    if (n_rows <= 0) return CLLM_OK;  // quant.cpp:1436
-    if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))
-        return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
-    if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
-    const int bsz = block_size_of(type);
-    if (in_dim % bsz != 0)
-        return fail(CLLM_ERR_BLOCK_MULTIPLE, "%s: in_dim not divisible by block size", fname);
-    if (!has_vec_dot_of(type))
-        return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
-    if (out_dim == 0) return CLLM_OK;
-    if (!y || (in_dim > 0 && (!x || !w))) return fail(CLLM_ERR_INVALID_ARG, "%s: null pointer", fname);
-    int dev;
-    if (int rc = ensure_device(&dev)) return rc;
-    const DeviceInfo& di = g_dev[dev];
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-
-    const int64_t row_bytes = (int64_t)(in_dim / bsz) * type_size_of(type);
-    const uint8_t* wd = static_cast<const uint8_t*>(w);
-    if (flags & CLLM_W_HOST) {
-        size_t avail = 0;
-        if (lookup(w, &wd, &avail) != CLLM_OK)
-            return fail(CLLM_ERR_NOT_REGISTERED, "%s: weight pointer %p is not inside a registered range",
-                        fname, w);
-        if ((uint64_t)row_bytes * (uint64_t)out_dim > avail)
-            return fail(CLLM_ERR_INVALID_ARG, "%s: weight matrix runs past its registered range", fname);
-    }
-
-    const bool use_tc = prefill_eligible(type, wd, row_bytes, in_dim, n_rows);
-    const int mchunk = std::min(n_rows, 8);
-    const ActLayout L = act_layout(use_tc ? 0 : mchunk, in_dim, 0);
-    size_t off_x = L.end, off_b = L.end, off_y = L.end, total = L.end;
-    if (flags & CLLM_X_HOST) {
-        off_x = total;
-        total = align256(total + (size_t)n_rows * in_dim * 4);
-        off_b = total;
-        if (bias) total = align256(total + (size_t)out_dim * 4);
-    }
-    if (flags & CLLM_Y_HOST) {
-        off_y = total;
-        total = align256(total + (size_t)n_rows * out_dim * 4);
-    }
-    const size_t off_pre = total;
-    if (use_tc) total += prefill_bytes(n_rows, in_dim);
-    const size_t off_img = total;
-    const bool want_image = !use_tc && in_dim >= kImageMinK;
-    if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
-    uint8_t* ws;
-    std::unique_lock<std::mutex> ws_lock;
-    if (int rc = workspace(dev, total, &ws, ws_lock)) return rc;
-
-    const float* xd = x;
-    const float* bd = bias;
-    float* yd = y;
-    if (flags & CLLM_X_HOST) {
-        xd = reinterpret_cast<float*>(ws + off_x);
-        CLLM_CUDA_TRY(cudaMemcpyAsync((void*)xd, x, (size_t)n_rows * in_dim * 4, cudaMemcpyHostToDevice, st));
-        if (bias) {
-            bd = reinterpret_cast<float*>(ws + off_b);
-            CLLM_CUDA_TRY(cudaMemcpyAsync((void*)bd, bias, (size_t)out_dim * 4, cudaMemcpyHostToDevice, st));
-        }
-    }
-    if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
-
-    if (use_tc) {
-        if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
-            return rc;
-    }
-    if (!use_tc) {
-        if (int rc = run_decode(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, nullptr, ws, L,
-                                want_image ? ws + off_img : nullptr, di, st))
-            return rc;
-    }
-    if (flags & CLLM_Y_HOST) {
-        CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
-        CLLM_CUDA_TRY(cudaStreamSynchronize(st));
-    }
-    return CLLM_OK;
+    return matmul_quant_impl(x, w, type, bias, in_dim, out_dim, n_rows, y, flags, static_cast<cudaStream_t>(stream),
+                             nullptr, 0, nullptr);
 }
 
 int cllm_cuda_matmul_q8(const float* scales, const int8_t* qs, const int32_t* bsums, const void* w,
@@ -872,9 +915,25 @@ int cllm_cuda_matmul_partials(const float* x, const void* w, int type, int in_di
                       static_cast<cudaStream_t>(stream));
 }
 
+int cllm_cuda_dequantize_f16(const void* src, int type, int64_t n, uint16_t* dst, void* stream) {
+    if (n < 0) return fail(CLLM_ERR_INVALID_ARG, "dequantize_f16: negative size");
+    if (!dequant_supported(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
+    if (n % block_size_of(type) != 0)
+        return fail(CLLM_ERR_BLOCK_MULTIPLE, "dequantize: n not divisible by block size");
+    if (n == 0) return CLLM_OK;
+    if (!src || !dst) return fail(CLLM_ERR_INVALID_ARG, "dequantize_f16: null pointer");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const int64_t grid = std::min<int64_t>((n + 255) / 256, 32LL * g_dev[dev].sms);
+    dequantize_f16_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t*>(src), type, n, dst);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
 int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream) {
     if (n < 0) return fail(CLLM_ERR_INVALID_ARG, "dequantize: negative size");
-    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
+    if (!dequant_supported(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
     if (n % block_size_of(type) != 0)
         return fail(CLLM_ERR_BLOCK_MULTIPLE, "dequantize: n not divisible by block size");
     if (n == 0) return CLLM_OK;
@@ -892,11 +951,19 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
                           int n_info) {
     if (!info || n_info < 0 || in_dim < 0 || out_dim < 0)
         return fail(CLLM_ERR_INVALID_ARG, "matmul_plan: bad arguments");
-    if (!has_vec_dot_of(type)) return fail(CLLM_ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type");
+    if (!has_vec_dot_of(type) && !dequant_supported(type))
+        return fail(CLLM_ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize");
     if (in_dim % block_size_of(type) != 0)
         return fail(CLLM_ERR_BLOCK_MULTIPLE, "matmul_quant: in_dim not divisible by block size");
     int dev;
     if (int rc = ensure_device(&dev)) return rc;
+    if (!has_vec_dot_of(type)) {  // the dequantize-and-float-dot fallback
+        const int rows_per_cta = kFallbackWarps * 32;
+        int vals[8] = {n_rows <= 0 ? 0 : (n_rows + 7) / 8, 3, 0, 32, 0, 0, (out_dim + rows_per_cta - 1) / rows_per_cta,
+                       (int)sizeof(float) * kFallbackWarps * 32 * 33};
+        for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];
+        return CLLM_OK;
+    }
     const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
     const int m = std::max(1, std::min(8, n_rows));
     const GemvPlan pl = plan_gemv(type, static_cast<const uint8_t*>(w), row_bytes, in_dim, out_dim, m, true,
@@ -1115,3 +1182,6 @@ int cllm_cuda_check_device_status(void) {
 }
 
 }  // extern "C"
+
+// The device-resident engine step (its own C ABI section of include/cllm_cuda.h).
+#include "engine.cuh"

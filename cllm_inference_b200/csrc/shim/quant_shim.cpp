@@ -1,8 +1,10 @@
 // The quant API of cllm_inference (include/cllm/core/quant.hpp in the
 // reference), implemented on the B200 library's C ABI (include/cllm_cuda.h).
 //
-// Every compute call runs on the GPU; the ThreadPool argument is accepted and
-// ignored.  Errors become std::runtime_error carrying the library's message,
+// Every compute call runs on the GPU, for all thirteen GGML types the
+// reference reads (types without an integer dot kernel take the reference's
+// dequantize-and-float-dot path, on the GPU); the ThreadPool argument is
+// accepted and ignored.  Errors become std::runtime_error carrying the library's message,
 // which reuses the reference's strings (quant.cpp:423, :1379, :1443, :1370).
 //
 // Weights: the engine passes pointers into the read-only GGUF mapping
@@ -99,9 +101,13 @@ size_t type_size(GgmlType type) { return static_cast<size_t>(cllm_cuda_type_size
 
 bool has_vec_dot(GgmlType type) { return cllm_cuda_has_vec_dot(static_cast<int>(type)) != 0; }
 
+// dequantize_block / dequantize_block_f16 for all thirteen types (quant.cpp
+// :371-402) on the GPU.  n need not fill the last block: the whole block is
+// uploaded and dequantized, and only n values come back.
 void dequantize_block(const void* src, float* dst, GgmlType type, int64_t n) {
     const int t = static_cast<int>(type);
-    if (!cllm_cuda_has_vec_dot(t)) throw std::runtime_error("unsupported ggml type for dequantize");
+    if (cllm_cuda_type_size(t) == 0) throw std::runtime_error("unsupported ggml type for dequantize");
+    if (n <= 0) return;
     ensure_init();
     const int bs = block_size(type);
     const size_t in_bytes = static_cast<size_t>((n + bs - 1) / bs) * type_size(type);
@@ -113,13 +119,17 @@ void dequantize_block(const void* src, float* dst, GgmlType type, int64_t n) {
 }
 
 void dequantize_block_f16(const void* src, uint16_t* dst, GgmlType type, int64_t n) {
-    if (type == GgmlType::F16) {
-        std::memcpy(dst, src, static_cast<size_t>(n) * sizeof(uint16_t));
-        return;
-    }
-    std::vector<float> tmp(static_cast<size_t>(n));
-    dequantize_block(src, tmp.data(), type, n);
-    for (int64_t i = 0; i < n; ++i) dst[i] = float_to_half(tmp[static_cast<size_t>(i)]);
+    const int t = static_cast<int>(type);
+    if (cllm_cuda_type_size(t) == 0) throw std::runtime_error("unsupported ggml type for dequantize");
+    if (n <= 0) return;
+    ensure_init();
+    const int bs = block_size(type);
+    const size_t in_bytes = static_cast<size_t>((n + bs - 1) / bs) * type_size(type);
+    const int64_t n_full = ((n + bs - 1) / bs) * bs;
+    DevBuf s(in_bytes), d(static_cast<size_t>(n_full) * sizeof(uint16_t));
+    to_dev(s.p, src, in_bytes);
+    check(cllm_cuda_dequantize_f16(s.p, t, n_full, d.as<uint16_t>(), nullptr));
+    to_host(dst, d.p, static_cast<size_t>(n) * sizeof(uint16_t));
 }
 
 std::vector<float> Tensor::dequantize() const {
@@ -178,7 +188,7 @@ void matmul_quant_batch(const float* x, const void* w, GgmlType type, const floa
     if (in_dim < 0 || bs <= 0 || in_dim % bs != 0)
         throw std::runtime_error(n_rows > 1 ? "matmul_quant_batch: in_dim not divisible by block size"
                                             : "matmul_quant: in_dim not divisible by block size");
-    if (!cllm_cuda_has_vec_dot(t)) throw std::runtime_error("vec_dot_row: no kernel for this type");
+    if (cllm_cuda_type_size(t) == 0) throw std::runtime_error("unsupported ggml type for dequantize");
     if (out_dim <= 0) return;
     ensure_init();
     const size_t bytes = static_cast<size_t>(in_dim / bs) * type_size(type) * static_cast<size_t>(out_dim);

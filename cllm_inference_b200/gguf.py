@@ -11,8 +11,9 @@ tensor into (gguf.cpp:171-189).  The model hyper-parameters come from the
 There are no model files in this build, so the engine tests and the decode
 benchmark write Llama-architecture files with seeded synthetic weights:
 
-* linear weights in GGML blocks (``synth.make_weights`` distributions), in a
-  Q4_K_M-style mix: attn_q/k/v/output, ffn_gate/up and token_embd Q4_K,
+* linear weights in GGML blocks (``synth.make_weights`` distributions, with
+  centred Q4_K mins so the values average about zero, as trained weights
+  do), in a Q4_K_M-style mix: attn_q/k/v/output, ffn_gate/up and token_embd Q4_K,
   ffn_down and output Q6_K (the shapes of BASELINE configs 2 and 4);
 * norm weights F32 ~ N(1, 0.1).
 
@@ -144,7 +145,7 @@ def tensor_data(name: str, t: int, rows: int, cols: int, seed: int) -> np.ndarra
     if t == F32:
         v = 1.0 + 0.1 * np.random.default_rng(s).standard_normal(rows * cols, dtype=np.float32)
         return v.astype(np.float32).view(np.uint8)
-    return synth.make_weights(t, rows, cols, seed=s)
+    return synth.make_weights(t, rows, cols, seed=s, centered=True)
 
 
 def write_llama(path: str, cfg: LlamaShape, seed: int = 0, down_type: int = synth.Q6_K) -> int:

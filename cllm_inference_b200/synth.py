@@ -27,9 +27,17 @@ from __future__ import annotations
 import numpy as np
 
 Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 6, 8, 12, 13, 14
-BLOCK = {Q4_0: 32, Q5_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
-TSIZE = {Q4_0: 18, Q5_0: 22, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
-NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+F32, F16, Q4_1, Q5_1, Q8_1, Q2_K, Q3_K = 0, 1, 3, 7, 9, 10, 11
+BLOCK = {Q4_0: 32, Q5_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256,
+         F32: 1, F16: 1, Q4_1: 32, Q5_1: 32, Q8_1: 32, Q2_K: 256, Q3_K: 256}
+TSIZE = {Q4_0: 18, Q5_0: 22, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210,
+         F32: 4, F16: 2, Q4_1: 20, Q5_1: 24, Q8_1: 36, Q2_K: 84, Q3_K: 110}
+NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K",
+         F32: "F32", F16: "F16", Q4_1: "Q4_1", Q5_1: "Q5_1", Q8_1: "Q8_1", Q2_K: "Q2_K", Q3_K: "Q3_K"}
+# fp16 fields of the fallback types: (byte offset, low, high) of a uniform draw
+_F16_FIELDS = {Q4_1: [(0, 1e-3, 2e-2), (2, -0.1, 0.1)], Q5_1: [(0, 1e-3, 2e-2), (2, -0.1, 0.1)],
+               Q8_1: [(0, 1e-3, 2e-2), (2, -1.0, 1.0)], Q2_K: [(80, 1e-3, 2e-2), (82, 0.0, 1e-2)],
+               Q3_K: [(108, 1e-3, 2e-2)]}
 BY_NAME = {v: k for k, v in NAMES.items()}
 
 
@@ -41,15 +49,41 @@ def _f16_bytes(vals: np.ndarray) -> np.ndarray:
     return vals.astype(np.float16).view(np.uint8).reshape(-1, 2)
 
 
-def make_weights(t: int, n_rows: int, k: int, seed: int) -> np.ndarray:
-    """[n_rows * row_bytes] uint8 of seeded synthetic blocks of type t."""
+def pack_scale_min_k4(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
+    """The 12 packed bytes of 8 six-bit (scale, min) pairs per super-block, as
+    get_scale_min_k4 (quant.cpp:72-80) unpacks them: sc, m [nblk, 8] in 0..63."""
+    sc = sc.astype(np.uint8)
+    m = m.astype(np.uint8)
+    out = np.empty((sc.shape[0], 12), np.uint8)
+    out[:, 0:4] = (sc[:, 0:4] & 63) | ((sc[:, 4:8] >> 4) << 6)
+    out[:, 4:8] = (m[:, 0:4] & 63) | ((m[:, 4:8] >> 4) << 6)
+    out[:, 8:12] = (sc[:, 4:8] & 0xF) | ((m[:, 4:8] & 0xF) << 4)
+    return out
+
+
+def make_weights(t: int, n_rows: int, k: int, seed: int, centered: bool = False) -> np.ndarray:
+    """[n_rows * row_bytes] uint8 of seeded synthetic blocks of type t.
+
+    centered=True (Q4_K/Q5_K only) draws every sub-block's min so that its
+    values average about zero, as trained weights do: dmin = 8 d and
+    m = round(sc * mean(q) / 8), mean(q) = 7.5 (Q4_K) or 15.5 (Q5_K, with
+    dmin = 16 d).  The engine's synthetic models use it; the GEMV benchmarks
+    keep the uniform scale/min bytes of the BASELINE distributions."""
     if k % BLOCK[t]:
         raise ValueError("k must be a multiple of the block size")
     rng = np.random.default_rng(seed)
     nblk = n_rows * (k // BLOCK[t])
+    if t == F32:
+        return rng.standard_normal(nblk, dtype=np.float32).view(np.uint8)
+    if t == F16:
+        return rng.standard_normal(nblk).astype(np.float16).view(np.uint8)
     ts = TSIZE[t]
     w = rng.integers(0, 256, size=(nblk, ts), dtype=np.uint8)
     if nblk == 0:
+        return w.reshape(-1)
+    if t in _F16_FIELDS:
+        for off, lo, hi in _F16_FIELDS[t]:
+            w[:, off:off + 2] = _f16_bytes(rng.uniform(lo, hi, size=nblk))
         return w.reshape(-1)
     d = rng.uniform(1e-3, 2e-2, size=nblk)
     if t == Q6_K:
@@ -58,7 +92,14 @@ def make_weights(t: int, n_rows: int, k: int, seed: int) -> np.ndarray:
     else:
         w[:, 0:2] = _f16_bytes(d)
         if t in (Q4_K, Q5_K):
-            w[:, 2:4] = _f16_bytes(rng.uniform(0.0, 1e-2, size=nblk))
+            if centered:
+                mean_q, ratio = (7.5, 8.0) if t == Q4_K else (15.5, 16.0)
+                sc = rng.integers(0, 64, size=(nblk, 8))
+                m = np.rint(sc * mean_q / ratio)
+                w[:, 2:4] = _f16_bytes(d.astype(np.float16).astype(np.float64) * ratio)
+                w[:, 4:16] = pack_scale_min_k4(sc, m)
+            else:
+                w[:, 2:4] = _f16_bytes(rng.uniform(0.0, 1e-2, size=nblk))
     return w.reshape(-1)
 
 

@@ -9,9 +9,12 @@
  * failure, using the reference's own exception strings where it has one.
  *
  * Weight types use the GGML numbering of GgmlType (quant.hpp:13-27).  The six
- * with an integer dot kernel (quant.hpp:129-130) are accepted by the matmul
- * entry points; every other type is rejected with CLLM_ERR_UNSUPPORTED_TYPE —
- * there is no CPU fallback.
+ * with an integer dot kernel (quant.hpp:129-130) run the quantized-activation
+ * path everywhere.  cllm_cuda_matmul_quant and cllm_cuda_dequantize also take
+ * the other seven types the reference reads (F32, F16, Q4_1, Q5_1, Q8_1, Q2_K,
+ * Q3_K) on the GPU, through the reference's dequantize-and-float-dot fallback
+ * (quant.cpp:1404-1430) computed in its exact order; any other type id is
+ * rejected with CLLM_ERR_UNSUPPORTED_TYPE — there is no CPU fallback.
  *
  * Streams are passed as `void*` (a cudaStream_t; NULL = the legacy default
  * stream).  Calls on one stream are not re-entrant: use one stream per engine.
@@ -38,6 +41,13 @@ extern "C" {
 #define CLLM_ERR_TOO_LARGE -8        /* a size beyond what an entry point supports */
 
 /* ---- GGML type ids (quant.hpp:13-27) ----------------------------------- */
+#define CLLM_TYPE_F32 0
+#define CLLM_TYPE_F16 1
+#define CLLM_TYPE_Q4_1 3
+#define CLLM_TYPE_Q5_1 7
+#define CLLM_TYPE_Q8_1 9
+#define CLLM_TYPE_Q2_K 10
+#define CLLM_TYPE_Q3_K 11
 #define CLLM_TYPE_Q4_0 2
 #define CLLM_TYPE_Q5_0 6
 #define CLLM_TYPE_Q8_0 8
@@ -136,15 +146,23 @@ int cllm_cuda_row_partials(const int8_t* qs, const void* w, int type, int in_dim
 int cllm_cuda_matmul_partials(const float* x, const void* w, int type, int in_dim, int out_dim, int n_rows,
                               int32_t* partials, void* stream);
 
-/* quant.cpp:371-389 (dequantize_block) for the six hot-path types: n values
- * from the blocks at src (device) into dst (device fp32).  Used by the
- * engine's embedding lookup (engine.cpp:310-316). */
+/* quant.cpp:371-389 (dequantize_block) for all thirteen types the reference
+ * handles: n values from the blocks at src (device) into dst (device fp32),
+ * bit-exact.  n must be a multiple of the block size.  Unknown types fail with
+ * "unsupported ggml type for dequantize".  Used by the engine's embedding
+ * lookup (engine.cpp:310-316) and its norm weights (engine.cpp:201-225). */
 int cllm_cuda_dequantize(const void* src, int type, int64_t n, float* dst, void* stream);
+
+/* quant.cpp:391-402 (dequantize_block_f16): as cllm_cuda_dequantize, then each
+ * value rounded to fp16 bits as the reference's float_to_half does
+ * (quant.hpp:58-85); F16 sources are copied. */
+int cllm_cuda_dequantize_f16(const void* src, int type, int64_t n, uint16_t* dst, void* stream);
 
 /* Launch plan cllm_cuda_matmul_quant would use for these arguments (device
  * weights at w): info[0] kernels launched per call, [1] the dot kernel: 0
  * direct loads, 1 bulk-copy (TMA) ring GEMV, 2 tcgen05 tensor-core GEMM
- * (Q4_K batches of >= 64 rows), [2] 1 if activation quantization is fused
+ * (Q4_K batches of >= 64 rows), 3 the dequantize-and-float-dot fallback
+ * (types without an integer dot kernel), [2] 1 if activation quantization is fused
  * into the dot kernel, [3] weight rows per tile, [4] warps per row, [5]
  * pipeline stages, [6] CTAs, [7] dynamic shared memory bytes.  No
  * counterpart in the reference; used by tests and the benchmark. */
@@ -235,6 +253,54 @@ int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int wor
  * Double-buffer y across consecutive calls: a rank may start writing call
  * n+1's slice while a slower rank still reads call n's y. */
 int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream);
+
+/* ---- Device-resident engine step ----------------------
+ * The reference's GgufLoader::load + TransformerEngine (gguf.cpp:120-275,
+ * engine.cpp:349-610, Llama architecture) with every activation in HBM: the
+ * GGUF data section is uploaded once in its native block layout, the
+ * quantized matmuls run through cllm_cuda_matmul_quant's kernels, RMSNorm,
+ * NEOX RoPE, GQA attention over an fp32 KV cache, SwiGLU, the residual adds
+ * and the greedy argmax (sampler.cpp:32-34) are GPU kernels, and one decode
+ * step is a CUDA graph that reads its token and position from device memory.
+ * The engine owns a CUDA stream; calls on one engine must not overlap (the
+ * reference engine is single-threaded too, http_server.cpp:715).  Models with
+ * per-head q/k norms (Qwen3), head_dim other than 64/128 or a GQA ratio other
+ * than 1/2/4/8 are rejected at creation. */
+
+/* GgufLoader::load + TransformerEngine(model, pool, Quant, ctx_limit):
+ * *engine receives an opaque handle.  ctx_limit > 0 caps the context as the
+ * reference does (engine.cpp:352-356). */
+int cllm_cuda_engine_create(const char* gguf_path, int ctx_limit, void** engine);
+int cllm_cuda_engine_destroy(void* engine);
+
+/* values[0..9]: n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab,
+ * n_ctx, kernel launches of one decode step (graph nodes), seq_len. */
+int cllm_cuda_engine_config(const void* engine, int* values, int n);
+
+/* TransformerEngine::forward(token) (engine.cpp:466-518): logits (host,
+ * vocab floats, may be NULL) and the greedy next token (may be NULL).
+ * "context length exceeded" (CLLM_ERR_TOO_LARGE) when the cache is full. */
+int cllm_cuda_engine_forward(void* engine, int token, float* logits, int* next_token);
+
+/* TransformerEngine::prefill(tokens) (engine.cpp:520-610), including its
+ * reuse of the cached prefix: the last token's logits and greedy next token. */
+int cllm_cuda_engine_prefill(void* engine, const int* tokens, int n, float* logits, int* next_token);
+
+/* Greedy generation on the device: prefill(prompt), then steps - 1 decode
+ * steps, each fed the previous step's argmax without a host round trip.
+ * tokens_out[steps] receives the generated tokens (the first is the
+ * prefill's argmax), margins_out[steps] (may be NULL) each token's logit
+ * minus the runner-up's.  Equivalent to the reference's greedy loop of
+ * prefill + forward(argmax) calls. */
+int cllm_cuda_engine_generate(void* engine, const int* prompt, int n_prompt, int steps, int* tokens_out,
+                              float* margins_out);
+
+/* TransformerEngine::reset_kv_cache / seq_len (engine.hpp:46-48). */
+int cllm_cuda_engine_reset(void* engine);
+int cllm_cuda_engine_seq_len(const void* engine);
+
+/* The engine's CUDA stream (for callers that time or order work around it). */
+int cllm_cuda_engine_stream(const void* engine, void** stream);
 
 /* Read and clear the device-side status word that kernels set when a bounded
  * wait expires (CLLM_ERR_KERNEL_TIMEOUT); synchronizes the device. */

@@ -26,8 +26,12 @@ ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libcllm_ref.so")
 
 Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 6, 8, 12, 13, 14
+F32, F16, Q4_1, Q5_1, Q8_1, Q2_K, Q3_K = 0, 1, 3, 7, 9, 10, 11
 HOT_TYPES = (Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K)
-TYPE_NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+OTHER_TYPES = (F32, F16, Q4_1, Q5_1, Q8_1, Q2_K, Q3_K)  # dequantize + float-dot fallback (quant.cpp:1404-1430)
+ALL_TYPES = OTHER_TYPES + HOT_TYPES
+TYPE_NAMES = {Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", F32: "F32",
+              F16: "F16", Q4_1: "Q4_1", Q5_1: "Q5_1", Q8_1: "Q8_1", Q2_K: "Q2_K", Q3_K: "Q3_K"}
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -65,6 +69,8 @@ class Oracle:
         lib.orc_matmul_quant_batch.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_int, _P, _P, _P, _P, _P]
         lib.orc_dequantize.argtypes = [_P, ctypes.c_int, _I64, _P]
+        lib.orc_matmul_fallback.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            _P, _P]
         self.lib = lib
 
     def block_size(self, t: int) -> int:
@@ -128,6 +134,21 @@ class Oracle:
             raise RuntimeError("matmul_quant: in_dim not divisible by block size")
         if rc:
             raise RuntimeError(f"oracle matmul failed ({rc})")
+        return (y, a) if with_abs else y
+
+    def matmul_fallback(self, x: np.ndarray, w: np.ndarray, t: int, k: int, n: int,
+                        bias: np.ndarray | None = None, with_abs: bool = False):
+        """matmul_quant(_batch) for a type without an integer dot kernel (the
+        reference's dequantize-then-float-dot path): y [M, N] (and the |term| sums)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+        m = x.shape[0]
+        y = np.empty((m, n), np.float32)
+        a = np.empty((m, n), np.float64)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        rc = self.lib.orc_matmul_fallback(_ptr(x), _ptr(np.ascontiguousarray(w, np.uint8)), t, _ptr(b), k, n, m,
+                                          _ptr(y), _ptr(a))
+        if rc:
+            raise RuntimeError(f"oracle fallback matmul failed ({rc})")
         return (y, a) if with_abs else y
 
     def dequantize(self, w: np.ndarray, t: int, n: int) -> np.ndarray:
@@ -225,3 +246,75 @@ class Reference:
 
 def reference_available() -> bool:
     return os.path.exists(REF_SO)
+
+
+REF_ENGINE_SO = os.path.join(HERE, "_ref", "libcllm_ref_engine.so")
+
+
+def reference_engine_available() -> bool:
+    return os.path.exists(REF_ENGINE_SO)
+
+
+class ReferenceEngine:
+    """The reference's own TransformerEngine (engine.cpp, gguf.cpp, quant.cpp),
+    built unmodified into oracle/_ref/libcllm_ref_engine.so (wrapper:
+    oracle/ref_engine_capi.cpp), on a GGUF file."""
+
+    def __init__(self, path: str, n_threads: int = 0, ctx_limit: int = 0, so: str = REF_ENGINE_SO):
+        if not os.path.exists(so):
+            raise FileNotFoundError(so)
+        lib = ctypes.CDLL(so)
+        lib.ref_engine_last_error.restype = ctypes.c_char_p
+        lib.ref_engine_create.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]
+        lib.ref_engine_destroy.argtypes = [_P]
+        lib.ref_engine_config.argtypes = [_P, _P]
+        lib.ref_engine_prefill.argtypes = [_P, _P, ctypes.c_int, _P, _P]
+        lib.ref_engine_forward.argtypes = [_P, ctypes.c_int, _P, _P]
+        lib.ref_engine_greedy.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P]
+        lib.ref_engine_reset.argtypes = [_P]
+        lib.ref_engine_seq_len.argtypes = [_P]
+        self.lib = lib
+        h = _P()
+        n_threads = n_threads or (os.cpu_count() or 1)
+        self._check(lib.ref_engine_create(path.encode(), n_threads, ctx_limit, ctypes.byref(h)))
+        self.h = h
+        cfg = np.zeros(8, np.int32)
+        lib.ref_engine_config(h, _ptr(cfg))
+        (self.n_layers, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff, self.vocab,
+         self.n_ctx) = (int(v) for v in cfg)
+
+    def _check(self, rc: int) -> None:
+        if rc:
+            raise RuntimeError(self.lib.ref_engine_last_error().decode())
+
+    def prefill(self, tokens) -> np.ndarray:
+        ids = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.vocab, np.float32)
+        tok = ctypes.c_int()
+        self._check(self.lib.ref_engine_prefill(self.h, _ptr(ids), len(ids), _ptr(logits), ctypes.byref(tok)))
+        return logits
+
+    def forward(self, token: int) -> np.ndarray:
+        logits = np.empty(self.vocab, np.float32)
+        nxt = ctypes.c_int()
+        self._check(self.lib.ref_engine_forward(self.h, int(token), _ptr(logits), ctypes.byref(nxt)))
+        return logits
+
+    def greedy(self, prompt, steps: int):
+        """(tokens, top-1 minus top-2 margins) of greedy decoding after prefill(prompt)."""
+        ids = np.ascontiguousarray(prompt, np.int32)
+        toks = np.empty(steps, np.int32)
+        margins = np.empty(steps, np.float32)
+        self._check(self.lib.ref_engine_greedy(self.h, _ptr(ids), len(ids), steps, _ptr(toks), _ptr(margins)))
+        return toks, margins
+
+    def reset(self) -> None:
+        self._check(self.lib.ref_engine_reset(self.h))
+
+    def seq_len(self) -> int:
+        return self.lib.ref_engine_seq_len(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ref_engine_destroy(self.h)
+            self.h = None

@@ -426,10 +426,91 @@ int orc_matmul_quant_batch(const float* x, const uint8_t* w, int t, const float*
     return 0;
 }
 
-/* Dequantization of the six hot-path types (quant.cpp:38-48, :55-68, :82-109,
- * :114-131, :236-... Q6_K :134-160, Q5_K :300-335); used by known-answer tests. */
+/* Dequantization of all thirteen types of dequantize_block (quant.cpp:371-389):
+ * F32 :28-30, F16 :33-36, Q8_0 :38-50, Q4_0 :55-68, Q4_K :82-109, Q5_0 :114-131,
+ * Q6_K :134-160, Q4_1 :163-177, Q5_1 :181-201, Q8_1 :204-215, Q2_K :219-249,
+ * Q3_K :253-296, Q5_K :300-335.  Returns -2 for any other type. */
 int orc_dequantize(const uint8_t* s, int t, int64_t n, float* dst) {
     switch (t) {
+        case T_F32:
+            memcpy(dst, s, (size_t)n * 4);
+            return 0;
+        case T_F16:
+            for (int64_t i = 0; i < n; ++i) dst[i] = f16at(s + 2 * i);
+            return 0;
+        case T_Q4_1:
+            for (int64_t i = 0; i < n; i += 32, s += 20) {
+                const float d = f16at(s), m = f16at(s + 2);
+                for (int j = 0; j < 16; ++j) {
+                    if (i + j < n) dst[i + j] = d * (s[4 + j] & 0xF) + m;
+                    if (i + j + 16 < n) dst[i + j + 16] = d * (s[4 + j] >> 4) + m;
+                }
+            }
+            return 0;
+        case T_Q5_1:
+            for (int64_t i = 0; i < n; i += 32, s += 24) {
+                const float d = f16at(s), m = f16at(s + 2);
+                uint32_t qh = (uint32_t)s[4] | ((uint32_t)s[5] << 8) | ((uint32_t)s[6] << 16) |
+                              ((uint32_t)s[7] << 24);
+                for (int j = 0; j < 16; ++j) {
+                    int q0 = (s[8 + j] & 0xF) | (((qh >> j) & 1) << 4);
+                    int q1 = (s[8 + j] >> 4) | (((qh >> (j + 16)) & 1) << 4);
+                    if (i + j < n) dst[i + j] = d * q0 + m;
+                    if (i + j + 16 < n) dst[i + j + 16] = d * q1 + m;
+                }
+            }
+            return 0;
+        case T_Q8_1:
+            for (int64_t i = 0; i < n; i += 32, s += 36) {
+                const float d = f16at(s);
+                for (int j = 0; j < 32 && i + j < n; ++j) dst[i + j] = d * (int8_t)s[4 + j];
+            }
+            return 0;
+        case T_Q2_K:
+            for (int64_t i = 0; i < n; i += 256, s += 84) {
+                const uint8_t* sc = s;
+                const uint8_t* q = s + 16;
+                const float d = f16at(s + 80), dmin = f16at(s + 82);
+                int is = 0;
+                for (int h = 0; h < 2; ++h, q += 32)
+                    for (int j = 0; j < 4; ++j)
+                        for (int part = 0; part < 2; ++part) {
+                            const uint8_t b = sc[is++];
+                            const float dl = d * (b & 0xF), ml = dmin * (b >> 4);
+                            for (int l = 0; l < 16; ++l) {
+                                const int64_t o = i + 128 * h + 32 * j + 16 * part + l;
+                                if (o < n) dst[o] = dl * ((q[16 * part + l] >> (2 * j)) & 3) - ml;
+                            }
+                        }
+            }
+            return 0;
+        case T_Q3_K:
+            for (int64_t i = 0; i < n; i += 256, s += 110) {
+                const uint8_t* hm = s;
+                const uint8_t* q = s + 32;
+                uint32_t a[4];
+                memcpy(a, s + 96, 12);
+                const float dall = f16at(s + 108);
+                const uint32_t t2 = a[2];
+                a[2] = ((a[0] >> 4) & 0x0f0f0f0fu) | (((t2 >> 4) & 0x03030303u) << 4);
+                a[3] = ((a[1] >> 4) & 0x0f0f0f0fu) | (((t2 >> 6) & 0x03030303u) << 4);
+                a[0] = (a[0] & 0x0f0f0f0fu) | (((t2 >> 0) & 0x03030303u) << 4);
+                a[1] = (a[1] & 0x0f0f0f0fu) | (((t2 >> 2) & 0x03030303u) << 4);
+                const int8_t* scl = (const int8_t*)a;
+                int is = 0;
+                uint8_t m = 1;
+                for (int h = 0; h < 2; ++h, q += 32)
+                    for (int j = 0; j < 4; ++j, m = (uint8_t)(m << 1))
+                        for (int part = 0; part < 2; ++part) {
+                            const float dl = dall * (scl[is++] - 32);
+                            for (int l = 0; l < 16; ++l) {
+                                const int idx = 16 * part + l;
+                                const int64_t o = i + 128 * h + 32 * j + idx;
+                                if (o < n) dst[o] = dl * (((q[idx] >> (2 * j)) & 3) - ((hm[idx] & m) ? 0 : 4));
+                            }
+                        }
+            }
+            return 0;
         case T_Q8_0:
             for (int64_t i = 0; i < n; i += 32, s += 34) {
                 float d = f16at(s);
@@ -520,4 +601,36 @@ int orc_dequantize(const uint8_t* s, int t, int64_t n, float* dst) {
             return 0;
     }
     return -2;
+}
+
+/* quant.cpp:1404-1430 — matmul_quant's fallback for types without an integer
+ * dot kernel: every row is dequantized in chunks of 512 values (rounded down to
+ * whole blocks) and accumulated as acc = bias (or 0), then acc += x[i] * w[i]
+ * in element order, the product rounded before the add (the reference build
+ * does not fuse this statement; checked bitwise against it).  abs_terms (may be NULL) receives
+ * |bias| + sum |x[i] * w[i]| per output (the tolerance denominator).  Rows of
+ * up to 65536 values. */
+int orc_matmul_fallback(const float* x, const uint8_t* w, int t, const float* bias, int in_dim, int out_dim,
+                        int n_rows, float* y, double* abs_terms) {
+    static float buf[65536];
+    const int bsz = orc_block_size(t);
+    if (orc_type_size(t) == 0) return -2;
+    if (in_dim % bsz != 0) return -1;
+    if (in_dim > 65536) return -3;
+    const int64_t row_bytes = (in_dim / bsz) * orc_type_size(t);
+    for (int j = 0; j < out_dim; ++j) {
+        if (orc_dequantize(w + (int64_t)j * row_bytes, t, in_dim, buf) != 0) return -2;
+        for (int r = 0; r < n_rows; ++r) {
+            const float* xr = x + (int64_t)r * in_dim;
+            float acc = bias ? bias[j] : 0.0f;
+            double a = bias ? fabs((double)bias[j]) : 0.0;
+            for (int i = 0; i < in_dim; ++i) {
+                acc = acc + xr[i] * buf[i];
+                a += fabs((double)xr[i] * (double)buf[i]);
+            }
+            y[(int64_t)r * out_dim + j] = acc;
+            if (abs_terms) abs_terms[(int64_t)r * out_dim + j] = a;
+        }
+    }
+    return 0;
 }

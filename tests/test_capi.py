@@ -34,7 +34,12 @@ def test_argument_errors_before_device(lib):
          _lib.ERR_BLOCK_MULTIPLE, "matmul_quant: in_dim not divisible by block size")
     _err(lib, lib.cllm_cuda_matmul_quant(dummy, dummy, 12, None, 100, 4, 2, dummy, 0, None),
          _lib.ERR_BLOCK_MULTIPLE, "matmul_quant_batch: in_dim not divisible by block size")
-    _err(lib, lib.cllm_cuda_matmul_quant(dummy, dummy, 3, None, 64, 4, 1, dummy, 0, None),
+    # the thirteen GGML types are accepted (the seven without an integer dot
+    # kernel on the dequantize fallback); other ids fail as the reference's
+    # fallback does, in dequantize_block (quant.cpp:387)
+    _err(lib, lib.cllm_cuda_matmul_quant(dummy, dummy, 4, None, 64, 4, 1, dummy, 0, None),
+         _lib.ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize")
+    _err(lib, lib.cllm_cuda_matmul_q8(dummy, dummy, dummy, dummy, 3, None, 64, 4, 1, dummy, None),
          _lib.ERR_UNSUPPORTED_TYPE, "vec_dot_row: no kernel for this type")
     _err(lib, lib.cllm_cuda_quantize_q8_0(dummy, 33, 1, dummy, dummy, dummy, None),
          _lib.ERR_BLOCK_MULTIPLE, "quantize_row_q8_0: n not divisible by 32")
@@ -42,7 +47,9 @@ def test_argument_errors_before_device(lib):
          _lib.ERR_INVALID_ARG, "unknown flags")
     _err(lib, lib.cllm_cuda_matmul_quant(dummy, dummy, 12, None, -256, 4, 1, dummy, 0, None),
          _lib.ERR_INVALID_ARG, "negative")
-    _err(lib, lib.cllm_cuda_dequantize(dummy, 3, 32, dummy, None),
+    _err(lib, lib.cllm_cuda_dequantize(dummy, 5, 32, dummy, None),
+         _lib.ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize")
+    _err(lib, lib.cllm_cuda_dequantize_f16(dummy, 99, 32, dummy, None),
          _lib.ERR_UNSUPPORTED_TYPE, "unsupported ggml type for dequantize")
     _err(lib, lib.cllm_cuda_register_weights(None, 0, None), _lib.ERR_INVALID_ARG, "empty range")
     # n_rows <= 0 and out_dim == 0 are no-ops (quant.cpp:1436); nothing is touched

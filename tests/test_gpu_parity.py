@@ -258,3 +258,44 @@ def test_production_partials_small_and_unaligned(cuda, lib, oracle):
             _, qs, _ = oracle.quantize(x)
             P = G.matmul_partials(lib, x, w, t, k, n)
             assert np.array_equal(P, oracle.partials(w, t, k, n, qs)), (TYPE_NAMES[t], k, n, m)
+
+
+# ---- the seven types without an integer dot kernel (quant.cpp:28-336, :1404-1430)
+from oracle.oracle import ALL_TYPES, OTHER_TYPES  # noqa: E402
+
+
+@pytest.mark.parametrize("t", ALL_TYPES, ids=[TYPE_NAMES[t] for t in ALL_TYPES])
+def test_dequantize_all_types_bit_exact(cuda, lib, oracle, t):
+    k, nrow = 512, 5
+    w = synth.make_weights(t, nrow, k, seed=30 + t)
+    _, wp = G.dev_bytes(w)
+    out = torch.empty(nrow * k, dtype=torch.float32, device="cuda")
+    _lib.check(lib.cllm_cuda_dequantize(wp, t, nrow * k, G.dptr(out), G.stream()))
+    out16 = torch.empty(nrow * k, dtype=torch.int16, device="cuda")
+    _lib.check(lib.cllm_cuda_dequantize_f16(wp, t, nrow * k, G.dptr(out16), G.stream()))
+    torch.cuda.synchronize()
+    ref = oracle.dequantize(w, t, nrow * k)
+    assert np.array_equal(bits(out.cpu().numpy()), bits(ref))
+    want16 = (np.ascontiguousarray(w).view(np.uint16) if t == synth.F16 else
+              np.array([oracle.float_to_half(float(v)) for v in ref], np.uint16))
+    assert np.array_equal(out16.cpu().numpy().view(np.uint16), want16)
+
+
+@pytest.mark.parametrize("t", OTHER_TYPES, ids=[TYPE_NAMES[t] for t in OTHER_TYPES])
+def test_fallback_matmul_bit_exact(cuda, lib, oracle, t):
+    """matmul_quant for the fallback types sums in the reference's order: bit-exact."""
+    for k, n, m in ((512, 37, 1), (4096, 300, 3), (1024, 129, 9)):
+        w = synth.make_weights(t, n, k, seed=k + n + t)
+        x = synth.make_activations(m, k, seed=m + t)
+        bias = np.linspace(-1, 1, n, dtype=np.float32) if m == 3 else None
+        y = G.matmul(lib, x, w, t, k, n, bias=bias)
+        yo = oracle.matmul_fallback(x, w, t, k, n, bias=bias)
+        assert np.array_equal(bits(y), bits(yo)), (TYPE_NAMES[t], k, n, m)
+
+
+def test_fallback_matches_reference_build(cuda, lib, reference):
+    for t in OTHER_TYPES:
+        k, n, m = 768, 50, 2
+        w = synth.make_weights(t, n, k, seed=7 * t)
+        x = synth.make_activations(m, k, seed=t)
+        assert np.array_equal(bits(G.matmul(lib, x, w, t, k, n)), bits(reference.matmul(x, w, t, k, n)))
