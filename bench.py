@@ -231,7 +231,19 @@ def cpu_baseline(target_s=10.0):
 # GPU arm
 
 
+T0 = time.perf_counter()
+
+
+def phase(msg):
+    """Progress line on stderr (the JSON result line goes to stdout)."""
+    print(f"[bench {time.perf_counter() - T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
+    import faulthandler
+
+    # a hung phase ends the run with every thread's Python stack on stderr
+    faulthandler.dump_traceback_later(int(os.environ.get("CLLM_BENCH_WATCHDOG_S", "1200")), exit=True)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -321,6 +333,7 @@ def main():
 
     # The sweep's 225 launches are captured once in a CUDA graph and replayed
     # per step, so the timed region measures the GPU, not Python launch cost.
+    phase("inputs resident; capturing the sweep graph")
     graph = capture_graph(torch, step)
     for _ in range(args.warmup):
         graph.replay()
@@ -378,6 +391,7 @@ def main():
 
     extra = {}
     if not args.quick:
+        phase("headline and roofline timed; secondary passes")
         extra = secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_call, calls, args)
 
     line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -396,6 +410,7 @@ def main():
         # BASELINE config 5 at this GPU count (a one-process group at N=1): the
         # row-sharded 70B sweep, with its parity check
         solo = dist is None
+        phase("row-sharded 70B sweep")
         if solo:
             dist = init_solo_group(torch, dev.index)
         line["sharded_70b"] = measure_70b(torch, dist, dev, world, rank, args.steps, args.warmup)
@@ -403,11 +418,13 @@ def main():
             dist.destroy_process_group()
             dist = None
     if not args.quick and rank == 0 and world == 1:
+        phase("engine: 8B decode step (config 4)")
         line["decode_8b"] = measure_engine(torch)
     line.update({k: v for k, v in extra.items() if k != "e2e"})
     if "e2e" in extra:
         line["e2e"] = extra["e2e"]
     if rank == 0 and not args.no_cpu_baseline and world == 1:
+        phase("CPU baseline (reference quant.cpp)")
         line["cpu_baseline"] = cpu_baseline()
     if dist is not None:
         dist.destroy_process_group()
@@ -559,8 +576,10 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         return float(tt.item())
 
+    phase("70B: weights resident; capturing")
     g = capture_graph(torch, lambda: run(calls))
     ms = timed(g, steps)
+    phase("70B: sweep timed")
     part = calls[:DISTINCT_70B * len(LAYER_70B)]
     g8 = capture_graph(torch, lambda: run(part))
     ms8 = timed(g8, steps)
@@ -571,6 +590,7 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
 
     _lib.check(_lib.load().cllm_cuda_check_device_status())
     del g, g8, g8n
+    phase("70B: parity check")
     parity = sharded_parity(torch, dist, grp, dev, world, rank)
     grp.close()
     return {"workload": "Llama-3-70B decode sweep (BASELINE config 5), M=1, row-sharded",
@@ -632,12 +652,15 @@ def measure_engine(torch, cfg_name="8b", n_prompt=512, steps=256, ctx=2048, cpu_
     d = tempfile.mkdtemp(dir=tmp_root)
     path = os.path.join(d, "llama3_8b_synthetic.gguf")
     try:
+        phase(f"engine: writing {path}")
         t0 = time.perf_counter()
         gguf.write_llama(path, shape, seed=8)
         t_write = time.perf_counter() - t0
         t0 = time.perf_counter()
+        phase("engine: loading")
         eng = Engine(path, ctx_limit=ctx)
         t_load = time.perf_counter() - t0
+        phase("engine: warm-up")
         st = torch.cuda.ExternalStream(eng.stream())
         prompt = [int(v) for v in np.random.default_rng(4).integers(3, shape.vocab, n_prompt)]
 
@@ -672,6 +695,7 @@ def measure_engine(torch, cfg_name="8b", n_prompt=512, steps=256, ctx=2048, cpu_
                                             "positions (mean context of the timed steps)"},
                "kernel_launches_per_decode_step": launches, "model_write_s": round(t_write, 1),
                "load_s": round(t_load, 1), "distinct_tokens": int(len(set(toks.tolist())))}
+        phase("engine: reference CPU sample")
         out["cpu_baseline"] = reference_engine_sample(path, cpu_steps)
         return out
     finally:
@@ -817,6 +841,7 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
         del ws
     out["per_shape_gbs"] = per
 
+    phase("prefill GEMM")
     # prefill: matmul_quant_batch 14336x4096 Q4_K
     pre = {}
     w = weights[(0, "gate")]
@@ -833,6 +858,7 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
                          "tops": round(2.0 * M * 14336 * 4096 / (ms * 1e-3) / 1e12, 2)}
     out["prefill_14336x4096_q4k"] = pre
 
+    phase("end-to-end sweep through host buffers")
     # e2e: the same sweep through the host-buffer C ABI call
     xh = {k: torch.from_numpy(synth.make_activations(1, k, k + 1)).pin_memory() for k in (4096, 14336)}
     yh = {n: torch.empty(n, dtype=torch.float32).pin_memory() for n in (4096, 1024, 14336, 128256)}

@@ -1,7 +1,7 @@
 // Device-resident engine step: the reference's GgufLoader::load + the
 // TransformerEngine (src/core/gguf.cpp:120-275, src/core/engine.cpp:349-610),
 // with the GGUF data section uploaded once to HBM in its native block layout
-// (cllm_cuda_register_weights) and every activation kept in device memory:
+// and every activation kept in device memory:
 // the quantized matmuls go through cllm_cuda_matmul_quant (device pointers),
 // the rest through engine_kernels.cuh.  One decode step (forward) is captured
 // in a CUDA graph that reads the input token and the position from device
@@ -184,8 +184,7 @@ struct Engine {
     int dev = 0;
     cudaStream_t st = nullptr;
     GgufFile file;
-    const uint8_t* data_host = nullptr;
-    uint8_t* data_dev = nullptr;
+    uint8_t* data_dev = nullptr;  // the file's data section in HBM
     Weight tok_embd, output;
     float* out_norm = nullptr;
     std::vector<Layer> layers;
@@ -228,7 +227,6 @@ struct Engine {
         if (part_acc) cudaFree(part_acc);
         if (tokens_dev) cudaFree(tokens_dev);
         if (host_state) cudaFreeHost(host_state);
-        if (data_host) cllm_cuda_unregister_weights(data_host);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -537,14 +535,15 @@ inline int create(const char* path, int ctx_limit, Engine** out) {
         return fail(CLLM_ERR_INVALID_ARG, "GQA ratio %d/%d is not supported", c.n_head, c.n_head_kv);
     CLLM_CUDA_TRY(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
 
-    // upload the data section once (gguf.cpp:178-189 points every tensor into it)
-    e->data_host = static_cast<const uint8_t*>(e->file.map) + e->file.data_off;
-    void* dbase = nullptr;
-    if (int rc = cllm_cuda_register_weights(e->data_host, e->file.size - e->file.data_off, &dbase)) {
-        e->data_host = nullptr;
-        return rc;
+    // upload the data section once (gguf.cpp:178-189 points every tensor into
+    // it), into the engine's own allocation: tensor offsets are multiples of
+    // the alignment (32), so every 16-byte-multiple row stays 16-byte aligned
+    {
+        const size_t bytes = e->file.size - e->file.data_off;
+        if (int rc = e->alloc(&e->data_dev, bytes)) return rc;
+        CLLM_CUDA_TRY(cudaMemcpy(e->data_dev, static_cast<const uint8_t*>(e->file.map) + e->file.data_off, bytes,
+                                 cudaMemcpyHostToDevice));
     }
-    e->data_dev = static_cast<uint8_t*>(dbase);
 
     if (c.vocab == 0) {  // gguf.cpp:270: the vocabulary size falls back to the embedding rows
         auto it = e->file.tensors.find("token_embd.weight");

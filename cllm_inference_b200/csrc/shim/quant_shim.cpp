@@ -20,6 +20,8 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <iterator>
+#include <map>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -70,6 +72,71 @@ bool in_readonly_mapping(const void* p, size_t bytes) {
     }
     std::fclose(f);
     return ro;
+}
+
+// Ranges this shim registered itself (one per weight matrix), with a
+// fingerprint of their first and last bytes.  A mapping can be unmapped and
+// its addresses reused by a later one (a model closed, another loaded); such
+// a stale registration is recognised when a call for the same matrix address
+// finds different bytes there, or when a new range overlaps it, and is then
+// dropped.  Ranges the caller registered (e.g. a whole data section) are the
+// caller's to manage.
+struct ShimRange {
+    size_t bytes;
+    uint8_t head[64], tail[64];
+};
+std::mutex g_ranges_mu;
+std::map<uintptr_t, ShimRange> g_ranges;
+
+size_t fp_len(size_t bytes) { return bytes < 64 ? bytes : 64; }
+
+bool fingerprint_matches(const ShimRange& r, const uint8_t* p) {
+    const size_t n = fp_len(r.bytes);
+    return std::memcmp(r.head, p, n) == 0 && std::memcmp(r.tail, p + r.bytes - n, n) == 0;
+}
+
+// Drop every shim registration that overlaps [a, a + bytes).
+void drop_overlapping(uintptr_t a, size_t bytes) {
+    auto it = g_ranges.lower_bound(a);
+    if (it != g_ranges.begin()) {
+        auto prev = std::prev(it);
+        if (prev->first + prev->second.bytes > a) it = prev;
+    }
+    while (it != g_ranges.end() && it->first < a + bytes) {
+        cllm_cuda_unregister_weights(reinterpret_cast<const void*>(it->first));
+        it = g_ranges.erase(it);
+    }
+}
+
+// Device copy of the weight matrix [w, w + bytes) when it can stay resident
+// (inside a registered range, or a read-only mapping registered now); nullptr
+// when the caller's memory is writable and must be uploaded per call.
+const void* resident_weights(const void* w, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_ranges_mu);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+    const auto* p = static_cast<const uint8_t*>(w);
+    auto it = g_ranges.find(a);
+    if (it != g_ranges.end() && (it->second.bytes != bytes || !fingerprint_matches(it->second, p))) drop_overlapping(a, bytes);
+    const void* dev = nullptr;
+    if (cllm_cuda_lookup_weights(w, &dev) == CLLM_OK) {
+        // a shim range that merely contains w but was made for another matrix
+        // is stale (matrices never overlap): drop it and look again
+        auto hit = g_ranges.upper_bound(a);
+        if (hit != g_ranges.begin() && (--hit)->first + hit->second.bytes > a && hit->first != a) {
+            drop_overlapping(a, bytes);
+            if (cllm_cuda_lookup_weights(w, &dev) != CLLM_OK) dev = nullptr;
+        }
+        if (dev) return w;  // resident: callers pass the host pointer with CLLM_W_HOST
+    }
+    if (!in_readonly_mapping(w, bytes)) return nullptr;
+    drop_overlapping(a, bytes);
+    check(cllm_cuda_register_weights(w, bytes, nullptr));
+    ShimRange r{bytes, {}, {}};
+    const size_t n = fp_len(bytes);
+    std::memcpy(r.head, p, n);
+    std::memcpy(r.tail, p + bytes - n, n);
+    g_ranges[a] = r;
+    return w;
 }
 
 // RAII device buffer for per-call staging (the reference API is synchronous).
@@ -192,12 +259,9 @@ void matmul_quant_batch(const float* x, const void* w, GgmlType type, const floa
     if (out_dim <= 0) return;
     ensure_init();
     const size_t bytes = static_cast<size_t>(in_dim / bs) * type_size(type) * static_cast<size_t>(out_dim);
-    const void* wd = nullptr;
-    if (bytes == 0 || cllm_cuda_lookup_weights(w, &wd) == CLLM_OK) {
-        check(cllm_cuda_matmul_quant(x, w, t, bias, in_dim, out_dim, n_rows, y,
-                                     CLLM_HOST_IO | (bytes ? CLLM_W_HOST : 0u), nullptr));
-    } else if (in_readonly_mapping(w, bytes)) {
-        check(cllm_cuda_register_weights(w, bytes, nullptr));
+    if (bytes == 0) {
+        check(cllm_cuda_matmul_quant(x, w, t, bias, in_dim, out_dim, n_rows, y, CLLM_HOST_IO, nullptr));
+    } else if (resident_weights(w, bytes)) {
         check(cllm_cuda_matmul_quant(x, w, t, bias, in_dim, out_dim, n_rows, y,
                                      CLLM_HOST_IO | CLLM_W_HOST, nullptr));
     } else {
