@@ -129,13 +129,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
     for (int r = 0; r < REP; ++r)
 #pragma unroll
         for (int j = 0; j < DPL; ++j) qr[r][j] = qs[r][sub * DPL + j];
-    for (int pp = 2 * warp + hf; pp < len; pp += 2 * (kAttnThreads / 32)) {
-        const float4* kr = reinterpret_cast<const float4*>(kc + (int64_t)(p0 + pp) * kv_dim + kvh * HD + sub * DPL);
+    // The loop bound is uniform across the warp (both 16-lane halves run the
+    // same trips; a half past the chunk's end computes on zeros and stores
+    // nothing), so the full-warp shuffles below always have every lane.
+    for (int base = 2 * warp; base < len; base += 2 * (kAttnThreads / 32)) {
+        const int pp = base + hf;
+        const bool valid = pp < len;
         float kv[DPL];
+        if (valid) {
+            const float4* kr = reinterpret_cast<const float4*>(kc + (int64_t)(p0 + pp) * kv_dim + kvh * HD + sub * DPL);
 #pragma unroll
-        for (int j = 0; j < DPL / 4; ++j) {
-            const float4 f = __ldg(kr + j);
-            kv[4 * j] = f.x; kv[4 * j + 1] = f.y; kv[4 * j + 2] = f.z; kv[4 * j + 3] = f.w;
+            for (int j = 0; j < DPL / 4; ++j) {
+                const float4 f = __ldg(kr + j);
+                kv[4 * j] = f.x; kv[4 * j + 1] = f.y; kv[4 * j + 2] = f.z; kv[4 * j + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) kv[j] = 0.0f;
         }
 #pragma unroll
         for (int r = 0; r < REP; ++r) {
@@ -144,7 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
             for (int j = 0; j < DPL; ++j) s = fmaf(qr[r][j], kv[j], s);
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-            if (sub == 0) es[r][pp] = __fmul_rn(s, scale);
+            if (valid && sub == 0) es[r][pp] = __fmul_rn(s, scale);
         }
     }
     __syncthreads();
