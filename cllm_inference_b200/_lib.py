@@ -68,6 +68,11 @@ SIGNATURES = {
     "cllm_cuda_engine_reset": (_I, [_P]),
     "cllm_cuda_engine_seq_len": (_I, [_P]),
     "cllm_cuda_engine_stream": (_I, [_P, ctypes.POINTER(_P)]),
+    "cllm_cuda_rms_norm": (_I, [_P, _P, _I, _I, ctypes.c_float, _P, _P]),
+    "cllm_cuda_silu_mul": (_I, [_P, _P, _I64, _P]),
+    "cllm_cuda_rope_table": (_I, [ctypes.c_float, _I, _I, _P]),
+    "cllm_cuda_rope_kv": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P]),
+    "cllm_cuda_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "cllm_cuda_check_device_status": (_I, []),
     "cllm_cuda_last_error": (_I, [ctypes.c_char_p, _SZ]),
 }

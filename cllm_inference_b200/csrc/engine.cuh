@@ -776,3 +776,86 @@ int cllm_cuda_engine_stream(const void* engine, void** stream) {
 }
 
 }  // extern "C"
+
+// ---- the engine's operators as standalone calls (device pointers) ---------
+extern "C" {
+
+int cllm_cuda_rms_norm(const float* x, const float* w, int n, int rows, float eps, float* y, void* stream) {
+    if (n <= 0 || rows < 0 || !x || !w || !y) return cllm::fail(CLLM_ERR_INVALID_ARG, "rms_norm: bad arguments");
+    if (rows == 0) return CLLM_OK;
+    cllm::eng::rmsnorm_kernel<<<rows, cllm::eng::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, w, n, eps, y);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+int cllm_cuda_silu_mul(float* g, const float* u, int64_t n, void* stream) {
+    if (n < 0 || (n > 0 && (!g || !u))) return cllm::fail(CLLM_ERR_INVALID_ARG, "silu_mul: bad arguments");
+    if (n == 0) return CLLM_OK;
+    cllm::eng::silu_mul_kernel<<<cllm::eng::grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, n);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+int cllm_cuda_rope_table(float rope_theta, int head_dim, int n_pos, float* table) {
+    if (head_dim <= 0 || head_dim % 2 || n_pos < 0 || !table) return cllm::fail(CLLM_ERR_INVALID_ARG, "rope_table: bad arguments");
+    const int half = head_dim / 2;
+    for (int pos = 0; pos < n_pos; ++pos)
+        for (int i = 0; i < half; ++i) {
+            const float theta = pos / std::pow(rope_theta, (float)i / half);  // engine.cpp:50
+            table[2 * ((size_t)pos * half + i)] = std::cos(theta);
+            table[2 * ((size_t)pos * half + i) + 1] = std::sin(theta);
+        }
+    return CLLM_OK;
+}
+
+int cllm_cuda_rope_kv(float* q, const float* k, const float* v, int n_tok, int n_head, int n_head_kv, int head_dim,
+                      const float* table, int pos0, float* k_cache, float* v_cache, void* stream) {
+    if (n_tok < 0 || n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 2048 || pos0 < 0 ||
+        !q || !k || !v || !table || !k_cache || !v_cache)
+        return cllm::fail(CLLM_ERR_INVALID_ARG, "rope_kv: bad arguments");
+    if (n_tok == 0) return CLLM_OK;
+    cllm::eng::rope_kv_kernel<<<dim3(n_tok, n_head + n_head_kv), head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
+        q, k, v, n_head, n_head_kv, head_dim, reinterpret_cast<const float2*>(table), nullptr, pos0, k_cache, v_cache);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+int cllm_cuda_attention(const float* q, const float* k_cache, const float* v_cache, int n_tok, int pos0, int n_head,
+                        int n_head_kv, int head_dim, float* out, void* stream) {
+    using namespace cllm;
+    if (n_tok <= 0 || pos0 < 0 || n_head <= 0 || n_head_kv <= 0 || !q || !k_cache || !v_cache || !out)
+        return fail(CLLM_ERR_INVALID_ARG, "attention: bad arguments");
+    if (head_dim != 64 && head_dim != 128) return fail(CLLM_ERR_INVALID_ARG, "attention: head_dim %d (64 or 128)", head_dim);
+    const int rep = n_head % n_head_kv == 0 ? n_head / n_head_kv : 0;
+    if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
+        return fail(CLLM_ERR_INVALID_ARG, "attention: GQA ratio %d/%d is not supported", n_head, n_head_kv);
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const int chunks = (pos0 + n_tok + eng::kAttnChunk - 1) / eng::kAttnChunk;
+    const size_t parts = (size_t)n_tok * n_head * chunks;
+    uint8_t* ws;
+    std::unique_lock<std::mutex> ws_lock;
+    if (int rc = workspace(dev, align256(parts * 2 * 4) + parts * head_dim * 4, &ws, ws_lock)) return rc;
+    float* ml = reinterpret_cast<float*>(ws);
+    float* acc = reinterpret_cast<float*>(ws + align256(parts * 2 * 4));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const float scale = 1.0f / std::sqrt((float)head_dim);
+    const dim3 grid(n_head_kv, chunks, n_tok);
+#define CLLM_ATTN_OP(HD, R) eng::attn_chunk_kernel<HD, R><<<grid, eng::kAttnThreads, 0, st>>>(q, k_cache, v_cache, n_head_kv, nullptr, pos0, scale, ml, acc)
+    if (head_dim == 128) {
+        if (rep == 1) CLLM_ATTN_OP(128, 1); else if (rep == 2) CLLM_ATTN_OP(128, 2);
+        else if (rep == 4) CLLM_ATTN_OP(128, 4); else CLLM_ATTN_OP(128, 8);
+        CLLM_CUDA_TRY(cudaGetLastError());
+        eng::attn_combine_kernel<128><<<dim3(n_head, n_tok), 128, 0, st>>>(ml, acc, chunks, nullptr, pos0, out);
+    } else {
+        if (rep == 1) CLLM_ATTN_OP(64, 1); else if (rep == 2) CLLM_ATTN_OP(64, 2);
+        else if (rep == 4) CLLM_ATTN_OP(64, 4); else CLLM_ATTN_OP(64, 8);
+        CLLM_CUDA_TRY(cudaGetLastError());
+        eng::attn_combine_kernel<64><<<dim3(n_head, n_tok), 64, 0, st>>>(ml, acc, chunks, nullptr, pos0, out);
+    }
+#undef CLLM_ATTN_OP
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+}  // extern "C"

@@ -11,9 +11,9 @@ tensor into (gguf.cpp:171-189).  The model hyper-parameters come from the
 There are no model files in this build, so the engine tests and the decode
 benchmark write Llama-architecture files with seeded synthetic weights:
 
-* linear weights in GGML blocks (``synth.make_weights`` distributions, with
-  centred Q4_K mins so the values average about zero, as trained weights
-  do), in a Q4_K_M-style mix: attn_q/k/v/output, ffn_gate/up and token_embd Q4_K,
+* linear weights in GGML blocks (``synth.make_weights``) with centred Q4_K
+  mins and block scales that give each matrix a value spread of about
+  1/sqrt(in_dim), as trained weights have, in a Q4_K_M-style mix: attn_q/k/v/output, ffn_gate/up and token_embd Q4_K,
   ffn_down and output Q6_K (the shapes of BASELINE configs 2 and 4);
 * norm weights F32 ~ N(1, 0.1).
 
@@ -139,13 +139,27 @@ def header_bytes(cfg: LlamaShape, plan) -> tuple[bytes, list[int], int]:
     return head + b"\0" * pad, offsets, off
 
 
+def weight_scale_range(t: int, cols: int):
+    """Block-scale range that gives a linear weight of `cols` inputs a value
+    spread of about 1/sqrt(cols), as in trained models, so activations stay
+    O(1) through the layers (the GEMV benchmarks' BASELINE scales are about
+    70x larger, which makes a stack of layers numerically chaotic: the
+    rounding differences of two correct implementations would decide the
+    greedy tokens).  Q4_K (centred): value ~ d * sc * (q - 7.5), spread about
+    145 d; Q6_K with |sc| <= 8: spread about 85 d."""
+    target = 1.0 / np.sqrt(cols)
+    mid = target / (145.0 if t == synth.Q4_K else 85.0)
+    return (0.5 * mid, 1.5 * mid)
+
+
 def tensor_data(name: str, t: int, rows: int, cols: int, seed: int) -> np.ndarray:
     """Seeded bytes of one tensor (a tensor's seed depends only on its name)."""
     s = (seed * 1000003 + sum((i + 1) * ord(c) for i, c in enumerate(name))) % (2 ** 63)
     if t == F32:
         v = 1.0 + 0.1 * np.random.default_rng(s).standard_normal(rows * cols, dtype=np.float32)
         return v.astype(np.float32).view(np.uint8)
-    return synth.make_weights(t, rows, cols, seed=s, centered=True)
+    return synth.make_weights(t, rows, cols, seed=s, centered=True, d_range=weight_scale_range(t, cols),
+                              q6_scale_max=8)
 
 
 def write_llama(path: str, cfg: LlamaShape, seed: int = 0, down_type: int = synth.Q6_K) -> int:

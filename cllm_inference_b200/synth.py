@@ -61,14 +61,17 @@ def pack_scale_min_k4(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
     return out
 
 
-def make_weights(t: int, n_rows: int, k: int, seed: int, centered: bool = False) -> np.ndarray:
+def make_weights(t: int, n_rows: int, k: int, seed: int, centered: bool = False, d_range=(1e-3, 2e-2),
+                 q6_scale_max: int = 32) -> np.ndarray:
     """[n_rows * row_bytes] uint8 of seeded synthetic blocks of type t.
 
     centered=True (Q4_K/Q5_K only) draws every sub-block's min so that its
     values average about zero, as trained weights do: dmin = 8 d and
     m = round(sc * mean(q) / 8), mean(q) = 7.5 (Q4_K) or 15.5 (Q5_K, with
     dmin = 16 d).  The engine's synthetic models use it; the GEMV benchmarks
-    keep the uniform scale/min bytes of the BASELINE distributions."""
+    keep the uniform scale/min bytes of the BASELINE distributions.
+    d_range: the uniform range of the block scale d (BASELINE: 1e-3..2e-2);
+    q6_scale_max: Q6_K sub-block scales are drawn from [-q6_scale_max, q6_scale_max)."""
     if k % BLOCK[t]:
         raise ValueError("k must be a multiple of the block size")
     rng = np.random.default_rng(seed)
@@ -85,9 +88,9 @@ def make_weights(t: int, n_rows: int, k: int, seed: int, centered: bool = False)
         for off, lo, hi in _F16_FIELDS[t]:
             w[:, off:off + 2] = _f16_bytes(rng.uniform(lo, hi, size=nblk))
         return w.reshape(-1)
-    d = rng.uniform(1e-3, 2e-2, size=nblk)
+    d = rng.uniform(d_range[0], d_range[1], size=nblk)
     if t == Q6_K:
-        w[:, 192:208] = rng.integers(-32, 32, size=(nblk, 16), dtype=np.int8).view(np.uint8)
+        w[:, 192:208] = rng.integers(-q6_scale_max, q6_scale_max, size=(nblk, 16), dtype=np.int8).view(np.uint8)
         w[:, 208:210] = _f16_bytes(d)
     else:
         w[:, 0:2] = _f16_bytes(d)

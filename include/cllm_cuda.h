@@ -302,6 +302,37 @@ int cllm_cuda_engine_seq_len(const void* engine);
 /* The engine's CUDA stream (for callers that time or order work around it). */
 int cllm_cuda_engine_stream(const void* engine, void** stream);
 
+/* ---- The engine step's operators as standalone calls ----------------------
+ * Device pointers, asynchronous on `stream`; the reference computes these on
+ * the host inside TransformerEngine.  Reductions (sums of squares, dot
+ * products, softmax sums) are trees, not the reference's loops. */
+
+/* rms_norm_ptr (engine.cpp:24-29) for `rows` rows of n:
+ * y = x * (1 / sqrt(sum(x^2) / n + eps)) * w. */
+int cllm_cuda_rms_norm(const float* x, const float* w, int n, int rows, float eps, float* y, void* stream);
+
+/* SwiGLU (engine.cpp:41, :511): g[i] = g[i] / (1 + exp(-g[i])) * u[i]. */
+int cllm_cuda_silu_mul(float* g, const float* u, int64_t n, void* stream);
+
+/* Host: the NEOX RoPE table of apply_rope (engine.cpp:44-57) -- (cos, sin) of
+ * pos / rope_theta^(i / (head_dim/2)) with the reference's float expressions,
+ * table[(pos * head_dim/2 + i) * 2 + {0,1}] for pos < n_pos. */
+int cllm_cuda_rope_table(float rope_theta, int head_dim, int n_pos, float* table);
+
+/* apply_rope on q (n_head heads) and k (n_head_kv heads) of n_tok tokens at
+ * positions pos0.. (engine.cpp:493-501), with the rotated k and v appended to
+ * the caches [position][n_head_kv * head_dim]; table: the device copy of
+ * cllm_cuda_rope_table's output covering those positions. */
+int cllm_cuda_rope_kv(float* q, const float* k, const float* v, int n_tok, int n_head, int n_head_kv, int head_dim,
+                      const float* table, int pos0, float* k_cache, float* v_cache, void* stream);
+
+/* GQA attention (engine.cpp:119-146) of n_tok query tokens at positions
+ * pos0.. (token t sees cache positions 0..pos0+t) over the fp32 caches:
+ * out[t][n_head * head_dim].  head_dim 64 or 128; GQA ratio 1, 2, 4 or 8.
+ * Partial results go to the library's workspace (see cllm_cuda_matmul_quant). */
+int cllm_cuda_attention(const float* q, const float* k_cache, const float* v_cache, int n_tok, int pos0, int n_head,
+                        int n_head_kv, int head_dim, float* out, void* stream);
+
 /* Read and clear the device-side status word that kernels set when a bounded
  * wait expires (CLLM_ERR_KERNEL_TIMEOUT); synchronizes the device. */
 int cllm_cuda_check_device_status(void);

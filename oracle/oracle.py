@@ -318,3 +318,48 @@ class ReferenceEngine:
         if self.h:
             self.lib.ref_engine_destroy(self.h)
             self.h = None
+
+
+REF_OPS_SO = os.path.join(HERE, "_ref", "libcllm_ref_ops.so")
+
+
+class ReferenceOps:
+    """The reference engine's internal operators (engine.cpp compiled whole into
+    oracle/ref_engine_ops.cpp -> oracle/_ref/libcllm_ref_ops.so)."""
+
+    def __init__(self, so: str = REF_OPS_SO):
+        if not os.path.exists(so):
+            raise FileNotFoundError(so)
+        lib = ctypes.CDLL(so)
+        lib.ref_op_rms_norm.argtypes = [_P, _P, ctypes.c_int, ctypes.c_float, _P]
+        lib.ref_op_silu.argtypes = [_P, _I64, _P]
+        lib.ref_op_rope.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]
+        lib.ref_op_attention.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
+        self.lib = lib
+
+    def rms_norm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.lib.ref_op_rms_norm(_ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), x.size, eps, _ptr(out))
+        return out
+
+    def silu(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.lib.ref_op_silu(_ptr(x), x.size, _ptr(out))
+        return out
+
+    def rope(self, q, n_head, head_dim, pos, theta):
+        q = np.array(q, np.float32, copy=True)
+        self.lib.ref_op_rope(_ptr(q), n_head, head_dim, pos, theta)
+        return q
+
+    def attention(self, q, kc, vc, seq, n_head, n_kv, head_dim):
+        out = np.empty(n_head * head_dim, np.float32)
+        self.lib.ref_op_attention(_ptr(np.ascontiguousarray(q, np.float32)), _ptr(np.ascontiguousarray(kc, np.float32)),
+                                  _ptr(np.ascontiguousarray(vc, np.float32)), seq, n_head, n_kv, head_dim, _ptr(out))
+        return out
+
+
+def reference_ops_available() -> bool:
+    return os.path.exists(REF_OPS_SO)
