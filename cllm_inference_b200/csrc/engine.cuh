@@ -288,6 +288,23 @@ inline int load_vector(Engine& e, const std::string& name, int n, bool optional,
     return cllm_cuda_dequantize(e.data_dev + t.offset, t.type, n, *out, e.st);
 }
 
+// Launch a kernel of the step with programmatic dependent launch (it starts
+// with griddepcontrol.wait, engine_kernels.cuh).
+template <class... KArgs, class... Args>
+inline int pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+    return CLLM_OK;
+}
+
 // A matmul of the engine: the decode step (n_rows == 1) runs on the engine's
 // own fixed scratch, prefill on the library's workspace.
 inline int mm(Engine& e, const float* x, const Weight& w, const float* bias, int n_rows, float* y) {
@@ -307,10 +324,11 @@ inline int launch_attention(Engine& e, const float* q, const float* kc, const fl
     const int rep = e.cfg.n_head / e.cfg.n_head_kv;
     const float scale = 1.0f / std::sqrt((float)e.cfg.head_dim);  // engine.cpp:126
     const dim3 grid(e.cfg.n_head_kv, n_chunks, T);
-#define CLLM_ATTN(R)                                                                                               \
-    case R:                                                                                                        \
-        attn_chunk_kernel<HD, R><<<grid, kAttnThreads, 0, e.st>>>(q, kc, vc, e.cfg.n_head_kv, pos_dev, pos0, scale, \
-                                                                  part_ml, part_acc);                            \
+#define CLLM_ATTN(R)                                                                                       \
+    case R:                                                                                                \
+        if (int rc_ = pdl(attn_chunk_kernel<HD, R>, grid, dim3(kAttnThreads), e.st, q, kc, vc, e.cfg.n_head_kv, \
+                          pos_dev, pos0, scale, part_ml, part_acc))                                        \
+            return rc_;                                                                                    \
         break;
     switch (rep) {
         CLLM_ATTN(1) CLLM_ATTN(2) CLLM_ATTN(4) CLLM_ATTN(8)
@@ -318,7 +336,7 @@ inline int launch_attention(Engine& e, const float* q, const float* kc, const fl
     }
 #undef CLLM_ATTN
     CLLM_CUDA_TRY(cudaGetLastError());
-    attn_combine_kernel<HD><<<dim3(e.cfg.n_head, T), HD, 0, e.st>>>(part_ml, part_acc, n_chunks, pos_dev, pos0, out);
+    if (int rc_ = pdl(attn_combine_kernel<HD>, dim3(dim3(e.cfg.n_head, T)), dim3(HD), e.st, part_ml, part_acc, n_chunks, pos_dev, pos0, out)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }
@@ -354,38 +372,38 @@ inline int ensure_parts(Engine& e, int T, int n_chunks) {
 inline int enqueue_step(Engine& e) {
     const Config& c = e.cfg;
     int* pos = e.state + kStatePos;
-    embed_kernel<<<dim3((c.n_embd + 255) / 256, 1), 256, 0, e.st>>>(
+    if (int rc_ = pdl(embed_kernel, dim3(dim3((c.n_embd + 255) / 256, 1)), dim3(256), e.st,
         e.tok_embd.dev, e.tok_embd.type,
         (int64_t)(c.n_embd / block_size_of(e.tok_embd.type)) * type_size_of(e.tok_embd.type), c.n_embd,
-        e.state + kStateToken, e.x);
+        e.state + kStateToken, e.x)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     const size_t kv_layer = (size_t)c.n_ctx * e.kv_dim();
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = e.layers[l];
-        rmsnorm_kernel<<<1, kNormThreads, 0, e.st>>>(e.x, L.attn_norm, c.n_embd, c.norm_eps, e.h);
+        if (int rc_ = pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), e.st, e.x, L.attn_norm, c.n_embd, c.norm_eps, e.h)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = mm(e, e.h, L.wq, L.bq, 1, e.q)) return rc;
         if (int rc = mm(e, e.h, L.wk, L.bk, 1, e.k)) return rc;
         if (int rc = mm(e, e.h, L.wv, L.bv, 1, e.v)) return rc;
         float* kc = e.kc + (size_t)l * kv_layer;
         float* vc = e.vc + (size_t)l * kv_layer;
-        rope_kv_kernel<<<dim3(1, c.n_head + c.n_head_kv), c.head_dim / 2, 0, e.st>>>(
-            e.q, e.k, e.v, c.n_head, c.n_head_kv, c.head_dim, e.rope, pos, 0, kc, vc);
+        if (int rc_ = pdl(rope_kv_kernel, dim3(dim3(1, c.n_head + c.n_head_kv)), dim3(c.head_dim / 2), e.st,
+            e.q, e.k, e.v, c.n_head, c.n_head_kv, c.head_dim, e.rope, pos, 0, kc, vc)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = attention(e, e.q, kc, vc, pos, 0, 1, e.n_chunks(), e.att)) return rc;
         if (int rc = mm(e, e.att, L.wo, e.x, 1, e.x)) return rc;  // x += W_o att (residual as the bias)
-        rmsnorm_kernel<<<1, kNormThreads, 0, e.st>>>(e.x, L.ffn_norm, c.n_embd, c.norm_eps, e.h);
+        if (int rc_ = pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), e.st, e.x, L.ffn_norm, c.n_embd, c.norm_eps, e.h)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = mm(e, e.h, L.wg, nullptr, 1, e.g)) return rc;
         if (int rc = mm(e, e.h, L.wu, nullptr, 1, e.u)) return rc;
-        silu_mul_kernel<<<grid_for(c.n_ff), 256, 0, e.st>>>(e.g, e.u, c.n_ff);
+        if (int rc_ = pdl(silu_mul_kernel, dim3(grid_for(c.n_ff)), dim3(256), e.st, e.g, e.u, c.n_ff)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = mm(e, e.g, L.wd, e.x, 1, e.x)) return rc;  // x += W_down swiglu
     }
-    rmsnorm_kernel<<<1, kNormThreads, 0, e.st>>>(e.x, e.out_norm, c.n_embd, c.norm_eps, e.h);
+    if (int rc_ = pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), e.st, e.x, e.out_norm, c.n_embd, c.norm_eps, e.h)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     if (int rc = mm(e, e.h, e.output, nullptr, 1, e.logits)) return rc;
-    argmax_kernel<<<1, kArgmaxThreads, 0, e.st>>>(e.logits, c.vocab, e.state, e.gen, e.margins, c.n_ctx, 1);
+    if (int rc_ = pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), e.st, e.logits, c.vocab, e.state, e.gen, e.margins, c.n_ctx, 1)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }
@@ -436,41 +454,41 @@ inline int run_prefill(Engine& e, const int* tokens, int T, int pos0) {
     const int chunks = (pos0 + T + kAttnChunk - 1) / kAttnChunk;
     if (int rc = ensure_parts(e, T, chunks)) return rc;
     CLLM_CUDA_TRY(cudaMemcpyAsync(e.tokens_dev, tokens, (size_t)T * sizeof(int), cudaMemcpyHostToDevice, e.st));
-    embed_kernel<<<dim3((c.n_embd + 255) / 256, T), 256, 0, e.st>>>(
+    if (int rc_ = pdl(embed_kernel, dim3(dim3((c.n_embd + 255) / 256, T)), dim3(256), e.st,
         e.tok_embd.dev, e.tok_embd.type,
         (int64_t)(c.n_embd / block_size_of(e.tok_embd.type)) * type_size_of(e.tok_embd.type), c.n_embd,
-        e.tokens_dev, e.X);
+        e.tokens_dev, e.X)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     const size_t kv_layer = (size_t)c.n_ctx * e.kv_dim();
     const int64_t ne = (int64_t)T * c.n_embd;
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = e.layers[l];
-        rmsnorm_kernel<<<T, kNormThreads, 0, e.st>>>(e.X, L.attn_norm, c.n_embd, c.norm_eps, e.H);
+        if (int rc_ = pdl(rmsnorm_kernel, dim3(T), dim3(kNormThreads), e.st, e.X, L.attn_norm, c.n_embd, c.norm_eps, e.H)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = mm(e, e.H, L.wq, L.bq, T, e.Q)) return rc;
         if (int rc = mm(e, e.H, L.wk, L.bk, T, e.K)) return rc;
         if (int rc = mm(e, e.H, L.wv, L.bv, T, e.V)) return rc;
         float* kc = e.kc + (size_t)l * kv_layer;
         float* vc = e.vc + (size_t)l * kv_layer;
-        rope_kv_kernel<<<dim3(T, c.n_head + c.n_head_kv), c.head_dim / 2, 0, e.st>>>(
-            e.Q, e.K, e.V, c.n_head, c.n_head_kv, c.head_dim, e.rope, nullptr, pos0, kc, vc);
+        if (int rc_ = pdl(rope_kv_kernel, dim3(dim3(T, c.n_head + c.n_head_kv)), dim3(c.head_dim / 2), e.st,
+            e.Q, e.K, e.V, c.n_head, c.n_head_kv, c.head_dim, e.rope, nullptr, pos0, kc, vc)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = attention(e, e.Q, kc, vc, nullptr, pos0, T, chunks, e.A)) return rc;
         if (int rc = mm(e, e.A, L.wo, nullptr, T, e.TMP)) return rc;
-        add_kernel<<<grid_for(ne), 256, 0, e.st>>>(e.X, e.TMP, ne);
-        rmsnorm_kernel<<<T, kNormThreads, 0, e.st>>>(e.X, L.ffn_norm, c.n_embd, c.norm_eps, e.H);
+        if (int rc_ = pdl(add_kernel, dim3(grid_for(ne)), dim3(256), e.st, e.X, e.TMP, ne)) return rc_;
+        if (int rc_ = pdl(rmsnorm_kernel, dim3(T), dim3(kNormThreads), e.st, e.X, L.ffn_norm, c.n_embd, c.norm_eps, e.H)) return rc_;
         if (int rc = mm(e, e.H, L.wg, nullptr, T, e.G)) return rc;
         if (int rc = mm(e, e.H, L.wu, nullptr, T, e.U)) return rc;
-        silu_mul_kernel<<<grid_for((int64_t)T * c.n_ff), 256, 0, e.st>>>(e.G, e.U, (int64_t)T * c.n_ff);
+        if (int rc_ = pdl(silu_mul_kernel, dim3(grid_for((int64_t)T * c.n_ff)), dim3(256), e.st, e.G, e.U, (int64_t)T * c.n_ff)) return rc_;
         if (int rc = mm(e, e.G, L.wd, nullptr, T, e.TMP)) return rc;
-        add_kernel<<<grid_for(ne), 256, 0, e.st>>>(e.X, e.TMP, ne);
+        if (int rc_ = pdl(add_kernel, dim3(grid_for(ne)), dim3(256), e.st, e.X, e.TMP, ne)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
     }
-    rmsnorm_kernel<<<1, kNormThreads, 0, e.st>>>(e.X + (size_t)(T - 1) * c.n_embd, e.out_norm, c.n_embd, c.norm_eps,
-                                                 e.h);
+    if (int rc_ = pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), e.st, e.X + (size_t)(T - 1) * c.n_embd, e.out_norm, c.n_embd, c.norm_eps,
+                                                 e.h)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     if (int rc = mm(e, e.h, e.output, nullptr, 1, e.logits)) return rc;
-    argmax_kernel<<<1, kArgmaxThreads, 0, e.st>>>(e.logits, c.vocab, e.state, e.gen, e.margins, c.n_ctx, T);
+    if (int rc_ = pdl(argmax_kernel, dim3(1), dim3(kArgmaxThreads), e.st, e.logits, c.vocab, e.state, e.gen, e.margins, c.n_ctx, T)) return rc_;
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }

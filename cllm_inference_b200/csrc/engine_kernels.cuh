@@ -32,6 +32,15 @@ constexpr int kArgmaxThreads = 1024;
 // a captured decode step can be replayed without host writes.
 enum : int { kStatePos = 0, kStateToken = 1, kStateCount = 2, kStateWords = 4 };
 
+// Programmatic dependent launch: every kernel of the step first waits for its
+// predecessor in the stream to complete (a no-op when launched without the
+// attribute), then lets its own successor be scheduled, so a kernel's launch
+// and prologue overlap the previous kernel's tail.
+__device__ __forceinline__ void pdl_start() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -47,6 +56,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // out[r] = x[r] * (1 / sqrt(sum(x[r]^2) / n + eps)) * w, one CTA per row r.
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                                int n, float eps, float* __restrict__ y) {
+    pdl_start();
     __shared__ float red[kNormThreads / 32];
     const float* xr = x + (int64_t)blockIdx.x * n;
     float* yr = y + (int64_t)blockIdx.x * n;
@@ -61,6 +71,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
 // as dequantize_block does.  grid (ceil(n/256), T).
 __global__ void embed_kernel(const uint8_t* __restrict__ table, int type, int64_t row_bytes, int n,
                              const int* __restrict__ tokens, float* __restrict__ x) {
+    pdl_start();
     const int t = blockIdx.y;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) x[(int64_t)t * n + i] = dequant_value(table + (int64_t)tokens[t] * row_bytes, type, i);
@@ -74,6 +85,7 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
                                int n_head, int n_kv, int hd, const float2* __restrict__ rope,
                                const int* __restrict__ pos_dev, int pos0, float* __restrict__ kc,
                                float* __restrict__ vc) {
+    pdl_start();
     const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x, half = hd >> 1;
     const int pos = (pos_dev ? *pos_dev : 0) + pos0 + t;
     const float2 cs = rope[(int64_t)pos * half + i];
@@ -110,6 +122,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
                                                                   const int* __restrict__ pos_dev, int pos0,
                                                                   float scale, float* __restrict__ part_ml,
                                                                   float* __restrict__ part_acc) {
+    pdl_start();
     constexpr int DPL = HD / 16;  // dims per lane (16 lanes per position)
     __shared__ float qs[REP][HD];
     __shared__ float es[REP][kAttnChunk];
@@ -206,6 +219,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
                                                           const float* __restrict__ part_acc, int n_chunks,
                                                           const int* __restrict__ pos_dev, int pos0,
                                                           float* __restrict__ out) {
+    pdl_start();
     const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x, n_head = gridDim.x;
     const int seq = (pos_dev ? *pos_dev : 0) + pos0 + t + 1;
     const int nc = (seq + kAttnChunk - 1) / kAttnChunk;
@@ -223,6 +237,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
 
 // g[i] = silu(g[i]) * u[i], silu(v) = v / (1 + exp(-v)).
 __global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+    pdl_start();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float v = g[i];
         g[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[i]);
@@ -231,6 +246,7 @@ __global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__
 
 // x[i] += t[i]
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ t, int64_t n) {
+    pdl_start();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         x[i] = __fadd_rn(x[i], t[i]);
 }
@@ -242,6 +258,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
                                                                 int* __restrict__ state, int* __restrict__ gen,
                                                                 float* __restrict__ margins, int gen_cap,
                                                                 int advance) {
+    pdl_start();
     __shared__ float sv1[kArgmaxThreads / 32], sv2[kArgmaxThreads / 32];
     __shared__ int si1[kArgmaxThreads / 32];
     float v1 = -INFINITY, v2 = -INFINITY;
