@@ -251,9 +251,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the per-shape, prefill and e2e passes")
-    ap.add_argument("--workload", default="8b", choices=["8b", "70b"],
+    ap.add_argument("--workload", default="8b", choices=["8b", "70b", "engine"],
                     help="8b: the decode sweep (headline, replicas per GPU); 70b: BASELINE config 5, every "
-                         "matrix row-sharded over the GPUs with the fused all-gather")
+                         "matrix row-sharded over the GPUs with the fused all-gather; engine: BASELINE config 4 "
+                         "alone (the device-resident 8B decode step; --steps = decode steps)")
     ap.add_argument("--shape", default=None,
                     help="profiling case TYPE:K:N:M (e.g. Q4_K:4096:14336:1): run only that matmul_quant "
                          "--steps times after --warmup, and print its timing")
@@ -265,6 +266,15 @@ def main():
         return run_shape(args)
     if args.workload == "70b":
         return run_70b(args)
+    if args.workload == "engine":
+        import torch
+
+        torch.cuda.set_device(0)
+        rec = measure_engine(torch, steps=max(args.steps, 2), cpu_steps=0 if args.no_cpu_baseline else 4)
+        print(json.dumps({"metric": "8B decode tok/s (BASELINE config 4)", "value": rec.get("decode_tok_s"),
+                          "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, **rec}))
+        return 0
 
     import torch
 
@@ -696,7 +706,7 @@ def measure_engine(torch, cfg_name="8b", n_prompt=512, steps=256, ctx=2048, cpu_
                "kernel_launches_per_decode_step": launches, "model_write_s": round(t_write, 1),
                "load_s": round(t_load, 1), "distinct_tokens": int(len(set(toks.tolist())))}
         phase("engine: reference CPU sample")
-        out["cpu_baseline"] = reference_engine_sample(path, cpu_steps)
+        out["cpu_baseline"] = reference_engine_sample(path, cpu_steps) if cpu_steps > 0 else None
         return out
     finally:
         shutil.rmtree(d, ignore_errors=True)
