@@ -255,6 +255,7 @@ def main():
                     help="8b: the decode sweep (headline, replicas per GPU); 70b: BASELINE config 5, every "
                          "matrix row-sharded over the GPUs with the fused all-gather; engine: BASELINE config 4 "
                          "alone (the device-resident 8B decode step; --steps = decode steps)")
+    ap.add_argument("--prompt", type=int, default=512, help="engine workload: prompt tokens before decoding")
     ap.add_argument("--shape", default=None,
                     help="profiling case TYPE:K:N:M (e.g. Q4_K:4096:14336:1): run only that matmul_quant "
                          "--steps times after --warmup, and print its timing")
@@ -270,7 +271,8 @@ def main():
         import torch
 
         torch.cuda.set_device(0)
-        rec = measure_engine(torch, steps=max(args.steps, 2), cpu_steps=0 if args.no_cpu_baseline else 4)
+        rec = measure_engine(torch, n_prompt=args.prompt, steps=max(args.steps, 2),
+                             cpu_steps=0 if args.no_cpu_baseline else 4)
         print(json.dumps({"metric": "8B decode tok/s (BASELINE config 4)", "value": rec.get("decode_tok_s"),
                           "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                           "higher_is_better": True, **rec}))
@@ -683,7 +685,7 @@ def measure_engine(torch, cfg_name="8b", n_prompt=512, steps=256, ctx=2048, cpu_
             return a.elapsed_time(b), out
 
         # warm-up: a short prefill + decode, then the timed runs from an empty cache
-        eng.generate(prompt[:80], 8)
+        eng.generate(prompt[:min(80, n_prompt)], 8)
         eng.reset()
         ms_pre, _ = timed(lambda: eng.prefill(prompt, logits=False))
         # generate() on the cached prompt re-runs only its last token (forward), then

@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -77,6 +78,11 @@ struct DeviceInfo {
     bool ready = false;
     int sms = 0;
     size_t max_smem_optin = 0;
+    // GEMV CTAs per SM of one call (1 or 2; environment CLLM_GEMV_CTAS_PER_SM).
+    // With 1, a second CTA slot stays free on every SM, so the next call's
+    // CTAs become resident while this one runs (programmatic dependent
+    // launch) and prefetch their first weight tiles.
+    int gemv_ctas_per_sm = 2;
 };
 
 std::mutex g_mu;
@@ -116,6 +122,7 @@ int ensure_device(int* out_dev) {
                         dev, prop.major, prop.minor);
         di.sms = prop.multiProcessorCount;
         di.max_smem_optin = prop.sharedMemPerBlockOptin;
+        if (const char* v = std::getenv("CLLM_GEMV_CTAS_PER_SM")) di.gemv_ctas_per_sm = std::atoi(v) == 1 ? 1 : 2;
         di.ready = true;
     }
     *out_dev = dev;
@@ -298,7 +305,7 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
         if (S < 2) S = 2;
         pl.stages = S;
         pl.smem = fixed + (size_t)S * pl.stage_bytes;
-        const int per_sm = pl.smem <= kSmemPerCta ? 2 : 1;
+        const int per_sm = pl.smem <= kSmemPerCta ? di.gemv_ctas_per_sm : 1;
         pl.grid = std::min(pl.num_tiles, per_sm * di.sms);
         // With few tiles per CTA, as few CTAs as keep the same number of tile
         // rounds: every CTA then gets the same number of tiles (within one),
