@@ -205,7 +205,7 @@ GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
     return nullptr;
 }
 
-typedef void (*ImageFn)(const float*, int, uint8_t*, const uint32_t*, const uint32_t*, int);
+typedef void (*ImageFn)(const float*, int, uint8_t*, const uint32_t*, const uint32_t*, int, const PreOp);
 
 template <int T>
 ImageFn image_fn(int m) {
@@ -246,7 +246,8 @@ uint32_t image_bytes(int m, int K) { return (uint32_t)kImageHeader + fused_act_b
 // wait_pad / wait_epoch / wait_world (row-sharded chains): wait for every rank's
 // announcement of round *wait_epoch before reading x; nullptr: no wait.
 int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas, cudaStream_t st,
-                 const uint32_t* wait_pad = nullptr, const uint32_t* wait_epoch = nullptr, int wait_world = 0) {
+                 const uint32_t* wait_pad = nullptr, const uint32_t* wait_epoch = nullptr, int wait_world = 0,
+                 PreOp pre = PreOp{kPreNone, nullptr, 0.0f}) {
     ImageFn fn = select_image(type, m);
     if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no activation-image kernel for type %d, %d rows", type, m);
     const int groups = (m * (K / 32) + kGemvThreads / 4 - 1) / (kGemvThreads / 4);
@@ -260,7 +261,7 @@ int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img, wait_pad, wait_epoch, wait_world));
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img, wait_pad, wait_epoch, wait_world, pre));
     *ctas = n;
     return CLLM_OK;
 }
@@ -552,7 +553,7 @@ int noalloc_scratch(int dev, uint8_t** out) {
 // 1 rows.
 int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, const float* bd, int in_dim,
                int out_dim, int n_rows, float* yd, int32_t* partials, uint8_t* ws, const ActLayout& L,
-               uint8_t* img, const DeviceInfo& di, cudaStream_t st) {
+               uint8_t* img, const DeviceInfo& di, cudaStream_t st, PreOp pre = PreOp{kPreNone, nullptr, 0.0f}) {
     const bool emit = partials != nullptr;
     const int64_t ppr = (type == kQ6_K ? 2 : 1) * (int64_t)(in_dim / 32);
     for (int t0 = 0; t0 < n_rows;) {
@@ -573,14 +574,18 @@ int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, 
         p.y = emit ? nullptr : yd + (size_t)t0 * out_dim;
         p.partials = emit ? partials + (size_t)t0 * out_dim * ppr : nullptr;
         fill_plan(p, pl);
+        if (pre.op != kPreNone && (!pl.fused || !pl.tma))
+            return fail(CLLM_ERR_INVALID_ARG, "matmul_quant: a pre-quantization step needs the fused GEMV");
         if (!pl.fused) {
             if (int rc = launch_quantize(p.x, in_dim, m, const_cast<float*>(p.dx), const_cast<int8_t*>(p.qx),
                                          const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
                 return rc;
         } else if (img && pl.tma) {
-            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st)) return rc;
+            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st, nullptr, nullptr, 0, pre)) return rc;
             p.image = img;
             p.image_bytes = image_bytes(m, in_dim);
+        } else {
+            p.pre = pre;
         }
         if (int rc = launch_gemv(type, emit, m, pl, p, st)) return rc;
         t0 += m;
@@ -594,7 +599,7 @@ int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, 
 // need != nullptr only the scratch size is computed (*need) and nothing runs.
 int matmul_quant_impl(const float* x, const void* w, int type, const float* bias, int in_dim, int out_dim,
                       int n_rows, float* y, unsigned flags, cudaStream_t st, uint8_t* scratch, size_t scratch_cap,
-                      size_t* need) {
+                      size_t* need, PreOp pre = PreOp{kPreNone, nullptr, 0.0f}) {
     const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
     if (n_rows <= 0) return CLLM_OK;  // quant.cpp:1436
     if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))
@@ -672,11 +677,13 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
         if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
             return rc;
     }
+    if (pre.op != kPreNone && (use_tc || fallback || (flags & CLLM_X_HOST)))
+        return fail(CLLM_ERR_INVALID_ARG, "%s: a pre-quantization step needs the fused GEMV", fname);
     if (fallback) {
         if (int rc = launch_fallback(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, st)) return rc;
     } else if (!use_tc) {
         if (int rc = run_decode(type, wd, row_bytes, xd, bd, in_dim, out_dim, n_rows, yd, nullptr, ws, L,
-                                want_image ? ws + off_img : nullptr, di, st))
+                                want_image ? ws + off_img : nullptr, di, st, pre))
             return rc;
     }
     if (flags & CLLM_Y_HOST) {

@@ -199,6 +199,13 @@ struct Engine {
     float *dpart_ml = nullptr, *dpart_acc = nullptr;  // decode attention partials (fixed: the graph uses them)
     uint8_t* scratch = nullptr;                       // decode matmul scratch (fixed: the graph uses it)
     size_t scratch_cap = 0;
+    // decode fusions (every decode matmul runs the fused GEMV): RMSNorm and
+    // SwiGLU inside the GEMVs' activation quantization, RoPE + KV append +
+    // attention + chunk merge in one kernel, multi-CTA argmax
+    bool fused = false;
+    int* attn_counters = nullptr;  // [n_head_kv], zero between steps
+    float* arg_part = nullptr;     // [kArgCtas][3]
+    int* arg_counter = nullptr;    // zero between steps
     int* state = nullptr;
     int* gen = nullptr;
     float* margins = nullptr;
@@ -313,6 +320,23 @@ inline int mm(Engine& e, const float* x, const Weight& w, const float* bias, int
                              decode ? e.scratch_cap : 0, nullptr);
 }
 
+// A decode matmul with a pre-quantization step (RMSNorm or SwiGLU) applied by
+// the GEMV itself.
+inline int mm_pre(Engine& e, const float* x, const Weight& w, const float* bias, float* y, PreOp pre) {
+    return matmul_quant_impl(x, w.dev, w.type, bias, w.cols, w.rows, 1, y, 0, e.st, e.scratch, e.scratch_cap, nullptr,
+                             pre);
+}
+
+// Whether a one-row matmul with w runs the fused GEMV (so pre-steps can ride on it).
+inline bool fusable(const Weight& w) {
+    if (!has_vec_dot_of(w.type)) return false;
+    int dev;
+    if (ensure_device(&dev)) return false;
+    const int64_t row_bytes = (int64_t)(w.cols / block_size_of(w.type)) * type_size_of(w.type);
+    const GemvPlan pl = plan_gemv(w.type, w.dev, row_bytes, w.cols, w.rows, 1, true, g_dev[dev]);
+    return pl.tma && pl.fused;
+}
+
 // Scratch bytes of a one-row matmul with w (matmul_quant_impl's size query).
 inline int scratch_need(const Weight& w, size_t* need) {
     return matmul_quant_impl(nullptr, w.dev, w.type, nullptr, w.cols, w.rows, 1, nullptr, 0, nullptr, nullptr, 0, need);
@@ -366,10 +390,60 @@ inline int ensure_parts(Engine& e, int T, int n_chunks) {
     return CLLM_OK;
 }
 
+template <int HD>
+inline int launch_attn_decode(Engine& e, float* kc, float* vc, const int* pos) {
+    const int rep = e.cfg.n_head / e.cfg.n_head_kv;
+    const float scale = 1.0f / std::sqrt((float)e.cfg.head_dim);  // engine.cpp:126
+    const dim3 grid(e.cfg.n_head_kv, e.n_chunks());
+#define CLLM_ATTN_DEC(R)                                                                                          \
+    case R:                                                                                                       \
+        return pdl(attn_decode_kernel<HD, R>, grid, dim3(kAttnThreads), e.st, e.q, e.k, e.v, kc, vc,              \
+                   e.cfg.n_head_kv, e.rope, pos, scale, e.dpart_ml, e.dpart_acc, e.attn_counters, e.att);
+    switch (rep) {
+        CLLM_ATTN_DEC(1) CLLM_ATTN_DEC(2) CLLM_ATTN_DEC(4) CLLM_ATTN_DEC(8)
+    }
+#undef CLLM_ATTN_DEC
+    return fail(CLLM_ERR_INVALID_ARG, "GQA ratio %d is not supported", rep);
+}
+
+// The decode step with its fusions (Engine::fused): per layer the q, k and v
+// GEMVs normalise x themselves, one attention kernel, the o GEMV adds into x,
+// the gate and up GEMVs normalise x, the down GEMV applies SwiGLU to its input
+// and adds into x; the output GEMV normalises; the argmax is spread over CTAs.
+inline int enqueue_step_fused(Engine& e) {
+    const Config& c = e.cfg;
+    int* pos = e.state + kStatePos;
+    if (int rc = pdl(embed_kernel, dim3((c.n_embd + 255) / 256, 1), dim3(256), e.st, e.tok_embd.dev, e.tok_embd.type,
+                     (int64_t)(c.n_embd / block_size_of(e.tok_embd.type)) * type_size_of(e.tok_embd.type), c.n_embd,
+                     (const int*)(e.state + kStateToken), e.x))
+        return rc;
+    const size_t kv_layer = (size_t)c.n_ctx * e.kv_dim();
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer& L = e.layers[l];
+        const PreOp n1{kPreRmsNorm, L.attn_norm, c.norm_eps}, n2{kPreRmsNorm, L.ffn_norm, c.norm_eps};
+        if (int rc = mm_pre(e, e.x, L.wq, L.bq, e.q, n1)) return rc;
+        if (int rc = mm_pre(e, e.x, L.wk, L.bk, e.k, n1)) return rc;
+        if (int rc = mm_pre(e, e.x, L.wv, L.bv, e.v, n1)) return rc;
+        float* kc = e.kc + (size_t)l * kv_layer;
+        float* vc = e.vc + (size_t)l * kv_layer;
+        const int rc_a = c.head_dim == 128 ? launch_attn_decode<128>(e, kc, vc, pos)
+                                           : launch_attn_decode<64>(e, kc, vc, pos);
+        if (rc_a) return rc_a;
+        if (int rc = mm(e, e.att, L.wo, e.x, 1, e.x)) return rc;  // x += W_o att
+        if (int rc = mm_pre(e, e.x, L.wg, nullptr, e.g, n2)) return rc;
+        if (int rc = mm_pre(e, e.x, L.wu, nullptr, e.u, n2)) return rc;
+        if (int rc = mm_pre(e, e.g, L.wd, e.x, e.x, PreOp{kPreSiluMul, e.u, 0.0f})) return rc;  // x += W_down swiglu
+    }
+    if (int rc = mm_pre(e, e.x, e.output, nullptr, e.logits, PreOp{kPreRmsNorm, e.out_norm, c.norm_eps})) return rc;
+    return pdl(argmax_multi_kernel, dim3(kArgCtas), dim3(256), e.st, (const float*)e.logits, c.vocab, e.arg_part,
+               e.arg_counter, e.state, e.gen, e.margins, c.n_ctx, 1);
+}
+
 // One decode step (engine.cpp:466-518) on e.st: embeds state[token] at
 // position state[pos], runs every layer, the output norm and matmul, and the
 // greedy argmax, which writes the next token and advances the position.
 inline int enqueue_step(Engine& e) {
+    if (e.fused) return enqueue_step_fused(e);
     const Config& c = e.cfg;
     int* pos = e.state + kStatePos;
     if (int rc_ = pdl(embed_kernel, dim3(dim3((c.n_embd + 255) / 256, 1)), dim3(256), e.st,
@@ -629,6 +703,15 @@ inline int create(const char* path, int ctx_limit, Engine** out) {
         }
         E.scratch_cap = std::max<size_t>(need, 256);
         if (int rc2 = E.alloc(&E.scratch, E.scratch_cap)) return rc2;
+        bool fz = E.output.dev != nullptr && fusable(E.output);
+        for (const Layer& L : E.layers)
+            for (const Weight* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) fz = fz && fusable(*w);
+        E.fused = fz && std::getenv("CLLM_ENGINE_UNFUSED") == nullptr;
+        if (int rc2 = E.alloc(&E.attn_counters, c.n_head_kv)) return rc2;
+        if (int rc2 = E.alloc(&E.arg_part, 3 * kArgCtas)) return rc2;
+        if (int rc2 = E.alloc(&E.arg_counter, 1)) return rc2;
+        CLLM_CUDA_TRY(cudaMemset(E.attn_counters, 0, c.n_head_kv * sizeof(int)));
+        CLLM_CUDA_TRY(cudaMemset(E.arg_counter, 0, sizeof(int)));
     }
     {
         const int half = c.head_dim / 2;

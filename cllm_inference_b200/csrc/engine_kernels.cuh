@@ -211,6 +211,148 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
     }
 }
 
+// The decode step's whole attention in one launch (T = 1, position *pos_dev):
+// every chunk CTA rotates the REP query heads it serves (apply_rope); the CTA
+// whose chunk holds this step's position also appends the rotated k and the v
+// of this token to the cache (no other CTA reads that row); then scores,
+// chunk softmax partials and e*v sums as attn_chunk_kernel; and the last CTA
+// of each KV head to finish (a counter per KV head, reset by that CTA) merges
+// the chunks as attn_combine_kernel.  Cache and partial reads in this kernel
+// use plain or L2 loads, never the read-only path: both are written here.
+template <int HD, int REP>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* __restrict__ q,
+                                                                   const float* __restrict__ k,
+                                                                   const float* __restrict__ v, float* kc, float* vc,
+                                                                   int n_kv, const float2* __restrict__ rope,
+                                                                   const int* __restrict__ pos_dev, float scale,
+                                                                   float* part_ml, float* part_acc, int* counters,
+                                                                   float* __restrict__ out) {
+    pdl_start();
+    constexpr int DPL = HD / 16, HALF = HD / 2;
+    __shared__ float qs[REP][HD];
+    __shared__ float es[REP][kAttnChunk];
+    __shared__ int s_last;
+    const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y;
+    const int kv_dim = n_kv * HD;
+    const int pos = *pos_dev, seq = pos + 1;
+    const int p0 = c * kAttnChunk;
+    if (p0 >= seq) return;
+    const int len = min(kAttnChunk, seq - p0);
+    const float2* cs = rope + (int64_t)pos * HALF;
+    for (int i = threadIdx.x; i < REP * HALF; i += kAttnThreads) {
+        const int r = i / HALF, j = i - r * HALF;
+        const float* qh = q + (kvh * REP + r) * HD;
+        const float x0 = qh[j], x1 = qh[j + HALF];
+        const float2 t = cs[j];
+        qs[r][j] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+        qs[r][j + HALF] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
+    }
+    if (pos < p0 + kAttnChunk) {  // this chunk holds the new position
+        for (int j = threadIdx.x; j < HALF; j += kAttnThreads) {
+            const float* kr = k + kvh * HD;
+            const float x0 = kr[j], x1 = kr[j + HALF];
+            const float2 t = cs[j];
+            float* kd = kc + (int64_t)pos * kv_dim + kvh * HD;
+            kd[j] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+            kd[j + HALF] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
+            float* vd = vc + (int64_t)pos * kv_dim + kvh * HD;
+            vd[j] = v[kvh * HD + j];
+            vd[j + HALF] = v[kvh * HD + j + HALF];
+        }
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 15, hf = lane >> 4;
+    float qr[REP][DPL];
+#pragma unroll
+    for (int r = 0; r < REP; ++r)
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) qr[r][j] = qs[r][sub * DPL + j];
+    for (int base = 2 * warp; base < len; base += 2 * (kAttnThreads / 32)) {  // warp-uniform bound
+        const int pp = base + hf;
+        const bool valid = pp < len;
+        float kv[DPL];
+        if (valid) {
+            const float4* kr = reinterpret_cast<const float4*>(kc + (int64_t)(p0 + pp) * kv_dim + kvh * HD + sub * DPL);
+#pragma unroll
+            for (int j = 0; j < DPL / 4; ++j) {
+                const float4 f = kr[j];
+                kv[4 * j] = f.x; kv[4 * j + 1] = f.y; kv[4 * j + 2] = f.z; kv[4 * j + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) kv[j] = 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < REP; ++r) {
+            float sc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) sc = fmaf(qr[r][j], kv[j], sc);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sc += __shfl_xor_sync(0xFFFFFFFFu, sc, o);
+            if (valid && sub == 0) es[r][pp] = __fmul_rn(sc, scale);
+        }
+    }
+    __syncthreads();
+    for (int r = warp; r < REP; r += kAttnThreads / 32) {
+        float m = -INFINITY;
+        for (int p = lane; p < len; p += 32) m = fmaxf(m, es[r][p]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        float l = 0.0f;
+        for (int p = lane; p < len; p += 32) {
+            const float e = expf(__fsub_rn(es[r][p], m));
+            es[r][p] = e;
+            l += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+        if (lane == 0) {
+            const int64_t pi = (int64_t)(kvh * REP + r) * n_chunks + c;
+            part_ml[2 * pi] = m;
+            part_ml[2 * pi + 1] = l;
+        }
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
+        float acc[REP];
+#pragma unroll
+        for (int r = 0; r < REP; ++r) acc[r] = 0.0f;
+        const float* vp = vc + (int64_t)p0 * kv_dim + kvh * HD + d;
+        for (int p = 0; p < len; ++p) {
+            const float vv = vp[(int64_t)p * kv_dim];
+#pragma unroll
+            for (int r = 0; r < REP; ++r) acc[r] = fmaf(es[r][p], vv, acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < REP; ++r) part_acc[((int64_t)(kvh * REP + r) * n_chunks + c) * HD + d] = acc[r];
+    }
+    // the last chunk CTA of this KV head merges every chunk's partials
+    __syncthreads();
+    const int nc = (seq + kAttnChunk - 1) / kAttnChunk;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(&counters[kvh], 1) == nc - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < REP * HD; i += kAttnThreads) {
+        const int h = kvh * REP + i / HD, d = i % HD;
+        const int64_t base = (int64_t)h * n_chunks;
+        float M = -INFINITY;
+        for (int cc = 0; cc < nc; ++cc) M = fmaxf(M, __ldcg(part_ml + 2 * (base + cc)));
+        float L = 0.0f, acc = 0.0f;
+        for (int cc = 0; cc < nc; ++cc) {
+            const float wgt = expf(__fsub_rn(__ldcg(part_ml + 2 * (base + cc)), M));
+            L = fmaf(wgt, __ldcg(part_ml + 2 * (base + cc) + 1), L);
+            acc = fmaf(wgt, __ldcg(part_acc + (base + cc) * HD + d), acc);
+        }
+        out[(int64_t)h * HD + d] = __fdiv_rn(acc, L);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0;
+}
+
 // Merge the chunks of attn_chunk_kernel: with M the largest chunk maximum and
 // w_c = exp(m_c - M), out[d] = sum_c w_c acc_c[d] / sum_c w_c l_c.
 // grid (n_head, T), block HD.
@@ -299,6 +441,78 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
         state[kStateCount] = c + 1;
         state[kStatePos] += advance;
     }
+}
+
+// Greedy sampling spread over kArgCtas CTAs: CTA b scans the b-th contiguous
+// slice of the logits; the last CTA to finish merges the slices in order (so a
+// tie still goes to the first index, as std::max_element) and does what
+// argmax_kernel does with the result.  The counter is reset by that CTA.
+constexpr int kArgCtas = 64;
+__global__ void __launch_bounds__(256) argmax_multi_kernel(const float* __restrict__ logits, int n, float* part,
+                                                           int* counter, int* __restrict__ state,
+                                                           int* __restrict__ gen, float* __restrict__ margins,
+                                                           int gen_cap, int advance) {
+    pdl_start();
+    __shared__ float sv1[8], sv2[8];
+    __shared__ int si1[8], s_last;
+    const int per = (n + kArgCtas - 1) / kArgCtas;
+    const int lo = blockIdx.x * per, hi = min(n, lo + per);
+    float v1 = -INFINITY, v2 = -INFINITY;
+    int i1 = 0x7FFFFFFF;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > v1) { v2 = v1; v1 = v; i1 = i; }
+        else if (v > v2) v2 = v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov1 = __shfl_xor_sync(0xFFFFFFFFu, v1, o), ov2 = __shfl_xor_sync(0xFFFFFFFFu, v2, o);
+        const int oi1 = __shfl_xor_sync(0xFFFFFFFFu, i1, o);
+        const bool other = ov1 > v1 || (ov1 == v1 && oi1 < i1);
+        const float lost = other ? v1 : ov1;
+        if (other) { v1 = ov1; i1 = oi1; }
+        v2 = fmaxf(fmaxf(v2, ov2), lost);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { sv1[w] = v1; sv2[w] = v2; si1[w] = i1; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b1 = sv1[0], b2 = sv2[0];
+        int bi = si1[0];
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k) {
+            const bool other = sv1[k] > b1 || (sv1[k] == b1 && si1[k] < bi);
+            const float lost = other ? b1 : sv1[k];
+            if (other) { b1 = sv1[k]; bi = si1[k]; }
+            b2 = fmaxf(fmaxf(b2, sv2[k]), lost);
+        }
+        part[3 * blockIdx.x] = b1;
+        part[3 * blockIdx.x + 1] = b2;
+        part[3 * blockIdx.x + 2] = __int_as_float(bi);
+        __threadfence();
+        s_last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last || threadIdx.x != 0) return;
+    __threadfence();
+    float b1 = __ldcg(part), b2 = __ldcg(part + 1);
+    int bi = __float_as_int(__ldcg(part + 2));
+    for (int k = 1; k < (int)gridDim.x; ++k) {
+        const float c1 = __ldcg(part + 3 * k), c2 = __ldcg(part + 3 * k + 1);
+        const int ci = __float_as_int(__ldcg(part + 3 * k + 2));
+        const bool other = c1 > b1 || (c1 == b1 && ci < bi);
+        const float lost = other ? b1 : c1;
+        if (other) { b1 = c1; bi = ci; }
+        b2 = fmaxf(fmaxf(b2, c2), lost);
+    }
+    state[kStateToken] = bi;
+    const int cnt = state[kStateCount];
+    if (cnt < gen_cap) {
+        gen[cnt] = bi;
+        margins[cnt] = b1 - b2;
+    }
+    state[kStateCount] = cnt + 1;
+    state[kStatePos] += advance;
+    *counter = 0;
 }
 
 }  // namespace eng

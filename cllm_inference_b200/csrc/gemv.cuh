@@ -26,6 +26,19 @@ constexpr int kMaxPeers = 8;  // GPUs of one node that a row-sharded call writes
 constexpr int kShardPadWords = 16;
 constexpr int kShardCountSlot = kMaxPeers;
 
+// An elementwise step applied to the fp32 activations just before their Q8_0
+// quantization, so the engine step needs no separate kernel for it:
+//   kPreRmsNorm  x = x * (1 / sqrt(sum(x^2) / K + eps)) * w   (rms_norm_ptr, engine.cpp:24-29)
+//   kPreSiluMul  x = x / (1 + exp(-x)) * w                    (SwiGLU, engine.cpp:41, :511)
+// w: the norm weight [K] (kPreRmsNorm) or the up-projection output [M][K]
+// (kPreSiluMul).  Only the fused and activation-image paths apply it.
+enum : int { kPreNone = 0, kPreRmsNorm = 1, kPreSiluMul = 2 };
+struct PreOp {
+    int op;
+    const float* w;
+    float eps;
+};
+
 struct GemvParams {
     const uint8_t* w;     // weight matrix, out_dim rows of row_bytes
     int64_t row_bytes;
@@ -60,6 +73,7 @@ struct GemvParams {
     const uint8_t* image;
     uint32_t image_bytes;
     int image_ctas;
+    PreOp pre;            // FUSED without image: applied by the CTA's own quantization
 };
 
 constexpr int kGemvWarps = 8;                      // warps that compute (R rows x wpr warps per row)
@@ -77,6 +91,7 @@ constexpr int kImageHeader = 128;  // image: u32 row masks of up to 32 quantizin
 constexpr int kImageMaxCtas = kImageHeader / 4;
 constexpr int kHdrCount = 256;     // 8 stages x 8 rows of int: warps of a row that finished the tile
 constexpr int kHdrRed = 512;       // 8 stages x 8 warps x 8 floats: partial row sums
+constexpr int kHdrPre = 3072;      // 8 warps x 8 rows of partial sums of squares, then 8 rms factors
 
 template <int T> struct TypeInfo;
 template <> struct TypeInfo<kQ4_0> { static constexpr int kBlock = 32, kBytes = 18, kUnitsPerBlock = 1; };
@@ -813,9 +828,57 @@ __device__ __forceinline__ void gemv_store_row(int j, const float (&acc)[M], con
 // every thread issues the loads of up to four blocks before reducing them.
 // x must be 16-byte aligned.  Returns the per-row "holds -128" mask.  Called
 // by all compute threads.
+// kPreRmsNorm: 1 / sqrt(sum(x[t]^2) / K + eps) of each of the M rows into
+// s_rms[t], computed by the kGemvThreads threads taking part (named barrier 1;
+// s_part holds 8 x M floats).  Every CTA sums in the same order, so every CTA
+// gets the same factors.
+template <int M>
+__device__ __forceinline__ void pre_rms(const float* __restrict__ x, int K, float eps, float* s_part, float* s_rms) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int t = 0; t < M; ++t) {
+        float s = 0.0f;
+        for (int i = tid; i < K; i += kGemvThreads) {
+            const float v = x[(int64_t)t * K + i];
+            s = fmaf(v, v, s);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (lane == 0) s_part[warp * M + t] = s;
+    }
+    named_barrier_sync(kGemvThreads);
+    if (tid < M) {
+        float sum = 0.0f;
+        for (int w = 0; w < kGemvThreads / 32; ++w) sum += s_part[w * M + tid];
+        s_rms[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)K), eps)));
+    }
+    named_barrier_sync(kGemvThreads);
+}
+
+// Apply the pre-quantization step to the eight values at x[t][k..k+7].
+__device__ __forceinline__ void pre_apply(const PreOp& pre, const float* s_rms, int t, int K, int k, float4& a,
+                                          float4& b) {
+    if (pre.op == kPreRmsNorm) {
+        const float r = s_rms[t];
+        const float4* w = reinterpret_cast<const float4*>(pre.w + k);
+        const float4 w0 = __ldg(w), w1 = __ldg(w + 1);
+        a = make_float4(__fmul_rn(__fmul_rn(a.x, r), w0.x), __fmul_rn(__fmul_rn(a.y, r), w0.y),
+                        __fmul_rn(__fmul_rn(a.z, r), w0.z), __fmul_rn(__fmul_rn(a.w, r), w0.w));
+        b = make_float4(__fmul_rn(__fmul_rn(b.x, r), w1.x), __fmul_rn(__fmul_rn(b.y, r), w1.y),
+                        __fmul_rn(__fmul_rn(b.z, r), w1.z), __fmul_rn(__fmul_rn(b.w, r), w1.w));
+    } else if (pre.op == kPreSiluMul) {
+        const float4* u = reinterpret_cast<const float4*>(pre.w + (int64_t)t * K + k);
+        const float4 u0 = __ldg(u), u1 = __ldg(u + 1);
+        auto sm = [](float v, float g) { return __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), g); };
+        a = make_float4(sm(a.x, u0.x), sm(a.y, u0.y), sm(a.z, u0.z), sm(a.w, u0.w));
+        b = make_float4(sm(b.x, u1.x), sm(b.y, u1.y), sm(b.z, u1.z), sm(b.w, u1.w));
+    }
+}
+
 template <int M, int TYPE, bool GLOBAL>
 __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x, int K, uint8_t* qs, float* dx,
-                                                    int* bs, int* hs, int gfirst, int gcount) {
+                                                    int* bs, int* hs, int gfirst, int gcount,
+                                                    const PreOp& pre, const float* s_rms) {
     // gfirst: this CTA's first group of blocks; gcount: groups per pass of all
     // CTAs taking part (one CTA: 0 and 64).  Returns this thread's row mask.
     const int kp = act_row_stride(K);
@@ -835,6 +898,7 @@ __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x,
                 const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t * K + 32 * b + 8 * sub);
                 v[u][0] = __ldg(src);
                 v[u][1] = __ldg(src + 1);
+                if (pre.op != kPreNone) pre_apply(pre, s_rms, t, K, 32 * b + 8 * sub, v[u][0], v[u][1]);
             } else {
                 v[u][0] = v[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
@@ -903,8 +967,9 @@ __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x,
 template <int M, int TYPE>
 __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
                                                      uint8_t* qs, float* dx, int* bs, int* hs,
-                                                     uint32_t* s_quirk) {
-    const uint32_t mask = quantize_blocks<M, TYPE, false>(x, K, qs, dx, bs, hs, 0, kGemvThreads / 4);
+                                                     uint32_t* s_quirk, const PreOp& pre, float* s_pre) {
+    if (pre.op == kPreRmsNorm) pre_rms<M>(x, K, pre.eps, s_pre, s_pre + 64);
+    const uint32_t mask = quantize_blocks<M, TYPE, false>(x, K, qs, dx, bs, hs, 0, kGemvThreads / 4, pre, s_pre + 64);
     // OR over the compute warps (*s_quirk is zero on entry), then a barrier
     // over those warps only: the producer warp does not take part.
     const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
@@ -922,8 +987,10 @@ __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x
 template <int M, int TYPE>
 __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __restrict__ x, int K,
                                                                  uint8_t* __restrict__ image, const uint32_t* wait_pad,
-                                                                 const uint32_t* wait_epoch, int wait_world) {
+                                                                 const uint32_t* wait_epoch, int wait_world,
+                                                                 const PreOp pre) {
     __shared__ uint32_t s_mask;
+    __shared__ float s_pre[64 + 8];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Row-sharded chain: x may be the previous round's all-gathered output, so
@@ -943,6 +1010,7 @@ __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __
     }
     if (threadIdx.x == 0) s_mask = 0;
     __syncthreads();
+    if (pre.op == kPreRmsNorm) pre_rms<M>(x, K, pre.eps, s_pre, s_pre + 64);
     const int nb = K >> 5;
     uint8_t* qs = image + kImageHeader;
     const uint32_t qbytes = (uint32_t)(M * act_row_stride(K));
@@ -950,7 +1018,7 @@ __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __
     int* bs = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
     int* hs = reinterpret_cast<int*>(qs + qbytes + 8u * (uint32_t)(M * nb));
     const uint32_t mask = quantize_blocks<M, TYPE, true>(x, K, qs, dx, bs, hs, (int)blockIdx.x * (kGemvThreads / 4),
-                                                         (int)gridDim.x * (kGemvThreads / 4));
+                                                         (int)gridDim.x * (kGemvThreads / 4), pre, s_pre + 64);
     const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
     if ((threadIdx.x & 31) == 0 && wm) atomicOr(&s_mask, wm);
     __syncthreads();
@@ -1062,7 +1130,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
             const uint32_t* masks = reinterpret_cast<const uint32_t*>(smem + kGemvSmemHeader - kImageHeader);
             for (int c = 0; c < p.image_ctas; ++c) qm |= masks[c];
         } else {
-            qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk);
+            qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk, p.pre,
+                                           reinterpret_cast<float*>(smem + kHdrPre));
         }
         quirk = (TYPE == kQ8_0 || TYPE == kQ6_K) ? qm : 0u;
         as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), smem_addr(hss), act_row_stride(p.K), nb};

@@ -234,3 +234,36 @@ def test_context_limit_and_errors(cuda, small_model):
     e.close()
     with pytest.raises(_lib.CudaError, match="cannot open model file"):
         Engine("/nonexistent/model.gguf")
+
+
+def test_fused_and_unfused_steps_agree(cuda, small_model):
+    """The fused decode step (RMSNorm/SwiGLU inside the GEMVs, one attention
+    kernel, multi-CTA argmax) against the unfused one (separate kernels,
+    CLLM_ENGINE_UNFUSED), teacher-forced on the same tokens: their norms sum in
+    different orders, so the bar is the re-quantization noise band, with the
+    greedy choice equal wherever the margin exceeds it."""
+    from cllm_inference_b200.engine import Engine
+
+    prompt = [3, 1000, 2000, 3000, 4000, 5000]
+    a = Engine(small_model[0])
+    os.environ["CLLM_ENGINE_UNFUSED"] = "1"
+    try:
+        b = Engine(small_model[0])
+    finally:
+        del os.environ["CLLM_ENGINE_UNFUSED"]
+    assert a.launches_per_step < b.launches_per_step
+    la, _ = a.prefill(prompt)
+    lb, tb = b.prefill(prompt)
+    decisive = agree = 0
+    for _ in range(24):
+        scale = float(np.max(np.abs(lb)))
+        assert np.max(np.abs(la - lb)) <= NOISE_BAND * scale
+        top = np.sort(lb)[-2:]
+        if top[1] - top[0] > NOISE_BAND * scale:
+            decisive += 1
+            agree += int(np.argmax(la) == np.argmax(lb))
+        la, _ = a.forward(tb)
+        lb, tb = b.forward(tb)
+    assert agree == decisive
+    a.close()
+    b.close()
