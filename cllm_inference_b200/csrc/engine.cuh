@@ -18,6 +18,7 @@
 #include <unistd.h>
 
 #include <cmath>
+#include <initializer_list>
 #include <memory>
 #include <unordered_map>
 
@@ -172,7 +173,29 @@ struct Layer {
     float* ffn_norm = nullptr;
     float *bq = nullptr, *bk = nullptr, *bv = nullptr;
     Weight wq, wk, wv, wo, wg, wu, wd;
+    // q|k|v and gate|up as one matrix each when the file stores them back to
+    // back with one type (one GEMV per group; rows = the parts' rows summed)
+    Weight wqkv, wgu;
 };
+
+inline uint64_t weight_bytes(const Weight& w) {
+    return (uint64_t)w.rows * (uint64_t)(w.cols / block_size_of(w.type)) * (uint64_t)type_size_of(w.type);
+}
+
+// w1 | w2 | ... as one matrix when contiguous, of one type and in_dim; else rows = 0.
+inline Weight group_weights(std::initializer_list<const Weight*> parts) {
+    Weight g = **parts.begin();
+    g.rows = 0;
+    const uint8_t* next = g.dev;
+    int rows = 0;
+    for (const Weight* w : parts) {
+        if (w->type != g.type || w->cols != g.cols || w->dev != next) return g;
+        next = w->dev + weight_bytes(*w);
+        rows += w->rows;
+    }
+    g.rows = rows;
+    return g;
+}
 
 struct Config {
     int n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab, n_ctx;
@@ -394,7 +417,7 @@ template <int HD>
 inline int launch_attn_decode(Engine& e, float* kc, float* vc, const int* pos) {
     const int rep = e.cfg.n_head / e.cfg.n_head_kv;
     const float scale = 1.0f / std::sqrt((float)e.cfg.head_dim);  // engine.cpp:126
-    const dim3 grid(e.cfg.n_head_kv, e.n_chunks());
+    const dim3 grid(e.cfg.n_head_kv, (e.cfg.n_ctx + kDecChunk - 1) / kDecChunk);
 #define CLLM_ATTN_DEC(R)                                                                                          \
     case R:                                                                                                       \
         return pdl(attn_decode_kernel<HD, R>, grid, dim3(kAttnThreads), e.st, e.q, e.k, e.v, kc, vc,              \
@@ -421,17 +444,25 @@ inline int enqueue_step_fused(Engine& e) {
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer& L = e.layers[l];
         const PreOp n1{kPreRmsNorm, L.attn_norm, c.norm_eps}, n2{kPreRmsNorm, L.ffn_norm, c.norm_eps};
-        if (int rc = mm_pre(e, e.x, L.wq, L.bq, e.q, n1)) return rc;
-        if (int rc = mm_pre(e, e.x, L.wk, L.bk, e.k, n1)) return rc;
-        if (int rc = mm_pre(e, e.x, L.wv, L.bv, e.v, n1)) return rc;
+        if (L.wqkv.rows) {  // e.q, e.k, e.v are contiguous: one GEMV writes all three
+            if (int rc = mm_pre(e, e.x, L.wqkv, nullptr, e.q, n1)) return rc;
+        } else {
+            if (int rc = mm_pre(e, e.x, L.wq, L.bq, e.q, n1)) return rc;
+            if (int rc = mm_pre(e, e.x, L.wk, L.bk, e.k, n1)) return rc;
+            if (int rc = mm_pre(e, e.x, L.wv, L.bv, e.v, n1)) return rc;
+        }
         float* kc = e.kc + (size_t)l * kv_layer;
         float* vc = e.vc + (size_t)l * kv_layer;
         const int rc_a = c.head_dim == 128 ? launch_attn_decode<128>(e, kc, vc, pos)
                                            : launch_attn_decode<64>(e, kc, vc, pos);
         if (rc_a) return rc_a;
         if (int rc = mm(e, e.att, L.wo, e.x, 1, e.x)) return rc;  // x += W_o att
-        if (int rc = mm_pre(e, e.x, L.wg, nullptr, e.g, n2)) return rc;
-        if (int rc = mm_pre(e, e.x, L.wu, nullptr, e.u, n2)) return rc;
+        if (L.wgu.rows) {  // e.g, e.u are contiguous
+            if (int rc = mm_pre(e, e.x, L.wgu, nullptr, e.g, n2)) return rc;
+        } else {
+            if (int rc = mm_pre(e, e.x, L.wg, nullptr, e.g, n2)) return rc;
+            if (int rc = mm_pre(e, e.x, L.wu, nullptr, e.u, n2)) return rc;
+        }
         if (int rc = mm_pre(e, e.g, L.wd, e.x, e.x, PreOp{kPreSiluMul, e.u, 0.0f})) return rc;  // x += W_down swiglu
     }
     if (int rc = mm_pre(e, e.x, e.output, nullptr, e.logits, PreOp{kPreRmsNorm, e.out_norm, c.norm_eps})) return rc;
@@ -674,12 +705,12 @@ inline int create(const char* path, int ctx_limit, Engine** out) {
     Engine& E = *e;
     int rc = E.alloc(&E.x, c.n_embd);
     if (!rc) rc = E.alloc(&E.h, c.n_embd);
-    if (!rc) rc = E.alloc(&E.q, qd);
-    if (!rc) rc = E.alloc(&E.k, kvd);
-    if (!rc) rc = E.alloc(&E.v, kvd);
+    if (!rc) rc = E.alloc(&E.q, (size_t)qd + 2 * kvd);  // q | k | v, one buffer
+    E.k = E.q + qd;
+    E.v = E.k + kvd;
     if (!rc) rc = E.alloc(&E.att, qd);
-    if (!rc) rc = E.alloc(&E.g, c.n_ff);
-    if (!rc) rc = E.alloc(&E.u, c.n_ff);
+    if (!rc) rc = E.alloc(&E.g, 2 * (size_t)c.n_ff);  // gate | up, one buffer
+    E.u = E.g + c.n_ff;
     if (!rc) rc = E.alloc(&E.logits, c.vocab);
     if (!rc) rc = E.alloc(&E.kc, (size_t)c.n_layers * c.n_ctx * kvd);
     if (!rc) rc = E.alloc(&E.vc, (size_t)c.n_layers * c.n_ctx * kvd);
@@ -690,13 +721,21 @@ inline int create(const char* path, int ctx_limit, Engine** out) {
     if (rc) return rc;
     CLLM_CUDA_TRY(cudaMallocHost(&E.host_state, kStateWords * sizeof(int)));
     {
-        const size_t parts = (size_t)c.n_head * E.n_chunks();
+        const size_t parts = (size_t)c.n_head * std::max(E.n_chunks(), (c.n_ctx + kDecChunk - 1) / kDecChunk);
         if (int rc2 = E.alloc(&E.dpart_ml, parts * 2)) return rc2;
         if (int rc2 = E.alloc(&E.dpart_acc, parts * c.head_dim)) return rc2;
         size_t need = 0, n1 = 0;
+        for (Layer& L : E.layers) {
+            const bool no_bias = !L.bq && !L.bk && !L.bv;
+            L.wqkv = no_bias ? group_weights({&L.wq, &L.wk, &L.wv}) : Weight{};
+            L.wgu = group_weights({&L.wg, &L.wu});
+        }
         std::vector<const Weight*> ws = {&E.output};
-        for (const Layer& L : E.layers)
+        for (const Layer& L : E.layers) {
             for (const Weight* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) ws.push_back(w);
+            if (L.wqkv.rows) ws.push_back(&L.wqkv);
+            if (L.wgu.rows) ws.push_back(&L.wgu);
+        }
         for (const Weight* w : ws) {
             if (int rc2 = scratch_need(*w, &n1)) return rc2;
             need = std::max(need, n1);
@@ -704,8 +743,11 @@ inline int create(const char* path, int ctx_limit, Engine** out) {
         E.scratch_cap = std::max<size_t>(need, 256);
         if (int rc2 = E.alloc(&E.scratch, E.scratch_cap)) return rc2;
         bool fz = E.output.dev != nullptr && fusable(E.output);
-        for (const Layer& L : E.layers)
+        for (const Layer& L : E.layers) {
             for (const Weight* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) fz = fz && fusable(*w);
+            if (L.wqkv.rows) fz = fz && fusable(L.wqkv);
+            if (L.wgu.rows) fz = fz && fusable(L.wgu);
+        }
         E.fused = fz && std::getenv("CLLM_ENGINE_UNFUSED") == nullptr;
         if (int rc2 = E.alloc(&E.attn_counters, c.n_head_kv)) return rc2;
         if (int rc2 = E.alloc(&E.arg_part, 3 * kArgCtas)) return rc2;
@@ -836,10 +878,10 @@ int cllm_cuda_engine_destroy(void* engine) {
 int cllm_cuda_engine_config(const void* engine, int* values, int n) {
     if (!engine || !values) return cllm::fail(CLLM_ERR_INVALID_ARG, "engine_config: null argument");
     const auto& c = static_cast<const Engine*>(engine)->cfg;
-    const int v[10] = {c.n_layers, c.n_embd, c.n_head, c.n_head_kv, c.head_dim, c.n_ff, c.vocab, c.n_ctx,
-                       (int)static_cast<const Engine*>(engine)->launches_per_step,
-                       static_cast<const Engine*>(engine)->seq_len};
-    for (int i = 0; i < n && i < 10; ++i) values[i] = v[i];
+    const Engine* e = static_cast<const Engine*>(engine);
+    const int v[11] = {c.n_layers, c.n_embd, c.n_head, c.n_head_kv, c.head_dim, c.n_ff, c.vocab, c.n_ctx,
+                       (int)e->launches_per_step, e->seq_len, e->fused ? 1 : 0};
+    for (int i = 0; i < n && i < 11; ++i) values[i] = v[i];
     return CLLM_OK;
 }
 

@@ -211,14 +211,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
     }
 }
 
-// The decode step's whole attention in one launch (T = 1, position *pos_dev):
-// every chunk CTA rotates the REP query heads it serves (apply_rope); the CTA
-// whose chunk holds this step's position also appends the rotated k and the v
-// of this token to the cache (no other CTA reads that row); then scores,
-// chunk softmax partials and e*v sums as attn_chunk_kernel; and the last CTA
-// of each KV head to finish (a counter per KV head, reset by that CTA) merges
-// the chunks as attn_combine_kernel.  Cache and partial reads in this kernel
-// use plain or L2 loads, never the read-only path: both are written here.
+// The decode step's whole attention in one launch (T = 1, position *pos_dev),
+// split over chunks of kDecChunk cache positions per KV head:
+//   * the chunk's K and V rows of this KV head are loaded into shared memory
+//     at once (every thread's loads in flight together: one memory latency);
+//   * each CTA rotates the REP query heads it serves (apply_rope); the CTA
+//     whose chunk holds this step's position also rotates the new k, writes it
+//     and v to the cache and into its tile (no other CTA reads that row);
+//   * scores, chunk maximum, exponentials, their sum and the e*v sums as
+//     attn_chunk_kernel;
+//   * the last CTA of each KV head to finish (a counter per KV head, reset by
+//     that CTA) merges the chunks as attn_combine_kernel.
+constexpr int kDecChunk = 32;
 template <int HD, int REP>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* __restrict__ q,
                                                                    const float* __restrict__ k,
@@ -228,16 +232,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* 
                                                                    float* part_ml, float* part_acc, int* counters,
                                                                    float* __restrict__ out) {
     pdl_start();
-    constexpr int DPL = HD / 16, HALF = HD / 2;
+    constexpr int HALF = HD / 2, RS = HD + 4;  // K/V tile row stride (floats): 16-byte rows, spread banks
+    __shared__ __align__(16) float ks[kDecChunk][RS];
+    __shared__ __align__(16) float vs[kDecChunk][RS];
     __shared__ float qs[REP][HD];
-    __shared__ float es[REP][kAttnChunk];
+    __shared__ float es[REP][kDecChunk];
     __shared__ int s_last;
     const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y;
     const int kv_dim = n_kv * HD;
     const int pos = *pos_dev, seq = pos + 1;
-    const int p0 = c * kAttnChunk;
+    const int p0 = c * kDecChunk;
     if (p0 >= seq) return;
-    const int len = min(kAttnChunk, seq - p0);
+    const int len = min(kDecChunk, seq - p0);
+    const bool holds_pos = pos < p0 + kDecChunk;
+    // K and V rows of the chunk (the new position's row comes from this step's k, v)
+    const int rows = holds_pos ? len - 1 : len;
+    constexpr int F4 = HD / 4;  // float4 per row
+    for (int i = threadIdx.x; i < rows * F4; i += kAttnThreads) {
+        const int r = i / F4, c4 = i - r * F4;
+        const int64_t g = (int64_t)(p0 + r) * kv_dim + kvh * HD + 4 * c4;
+        *reinterpret_cast<float4*>(&ks[r][4 * c4]) = *reinterpret_cast<const float4*>(kc + g);
+        *reinterpret_cast<float4*>(&vs[r][4 * c4]) = *reinterpret_cast<const float4*>(vc + g);
+    }
     const float2* cs = rope + (int64_t)pos * HALF;
     for (int i = threadIdx.x; i < REP * HALF; i += kAttnThreads) {
         const int r = i / HALF, j = i - r * HALF;
@@ -247,64 +263,55 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* 
         qs[r][j] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
         qs[r][j + HALF] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
     }
-    if (pos < p0 + kAttnChunk) {  // this chunk holds the new position
+    if (holds_pos) {
+        const int r = pos - p0;
         for (int j = threadIdx.x; j < HALF; j += kAttnThreads) {
             const float* kr = k + kvh * HD;
             const float x0 = kr[j], x1 = kr[j + HALF];
             const float2 t = cs[j];
+            const float k0 = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+            const float k1 = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
+            const float v0 = v[kvh * HD + j], v1 = v[kvh * HD + j + HALF];
             float* kd = kc + (int64_t)pos * kv_dim + kvh * HD;
-            kd[j] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
-            kd[j + HALF] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
             float* vd = vc + (int64_t)pos * kv_dim + kvh * HD;
-            vd[j] = v[kvh * HD + j];
-            vd[j + HALF] = v[kvh * HD + j + HALF];
+            kd[j] = k0;
+            kd[j + HALF] = k1;
+            vd[j] = v0;
+            vd[j + HALF] = v1;
+            ks[r][j] = k0;
+            ks[r][j + HALF] = k1;
+            vs[r][j] = v0;
+            vs[r][j + HALF] = v1;
         }
     }
     __syncthreads();
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 15, hf = lane >> 4;
-    float qr[REP][DPL];
-#pragma unroll
-    for (int r = 0; r < REP; ++r)
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) qr[r][j] = qs[r][sub * DPL + j];
-    for (int base = 2 * warp; base < len; base += 2 * (kAttnThreads / 32)) {  // warp-uniform bound
-        const int pp = base + hf;
-        const bool valid = pp < len;
-        float kv[DPL];
-        if (valid) {
-            const float4* kr = reinterpret_cast<const float4*>(kc + (int64_t)(p0 + pp) * kv_dim + kvh * HD + sub * DPL);
-#pragma unroll
-            for (int j = 0; j < DPL / 4; ++j) {
-                const float4 f = kr[j];
-                kv[4 * j] = f.x; kv[4 * j + 1] = f.y; kv[4 * j + 2] = f.z; kv[4 * j + 3] = f.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) kv[j] = 0.0f;
-        }
-#pragma unroll
-        for (int r = 0; r < REP; ++r) {
+    // scores: thread (position p, head r) for p < len, REP * kDecChunk <= 4 * 128
+    for (int i = threadIdx.x; i < REP * kDecChunk; i += kAttnThreads) {
+        const int r = i / kDecChunk, p = i - r * kDecChunk;
+        if (p < len) {
             float sc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) sc = fmaf(qr[r][j], kv[j], sc);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) sc += __shfl_xor_sync(0xFFFFFFFFu, sc, o);
-            if (valid && sub == 0) es[r][pp] = __fmul_rn(sc, scale);
+#pragma unroll 8
+            for (int d4 = 0; d4 < F4; ++d4) {
+                const float4 kk = *reinterpret_cast<const float4*>(&ks[p][4 * d4]);
+                const float4 qq = *reinterpret_cast<const float4*>(&qs[r][4 * d4]);
+                sc = fmaf(qq.x, kk.x, sc);
+                sc = fmaf(qq.y, kk.y, sc);
+                sc = fmaf(qq.z, kk.z, sc);
+                sc = fmaf(qq.w, kk.w, sc);
+            }
+            es[r][p] = __fmul_rn(sc, scale);
         }
     }
     __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int r = warp; r < REP; r += kAttnThreads / 32) {
-        float m = -INFINITY;
-        for (int p = lane; p < len; p += 32) m = fmaxf(m, es[r][p]);
+        const float sv = lane < len ? es[r][lane] : -INFINITY;
+        float m = sv;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-        float l = 0.0f;
-        for (int p = lane; p < len; p += 32) {
-            const float e = expf(__fsub_rn(es[r][p], m));
-            es[r][p] = e;
-            l += e;
-        }
+        const float e = lane < len ? expf(__fsub_rn(sv, m)) : 0.0f;
+        if (lane < len) es[r][lane] = e;
+        float l = e;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
         if (lane == 0) {
@@ -318,9 +325,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* 
         float acc[REP];
 #pragma unroll
         for (int r = 0; r < REP; ++r) acc[r] = 0.0f;
-        const float* vp = vc + (int64_t)p0 * kv_dim + kvh * HD + d;
         for (int p = 0; p < len; ++p) {
-            const float vv = vp[(int64_t)p * kv_dim];
+            const float vv = vs[p][d];
 #pragma unroll
             for (int r = 0; r < REP; ++r) acc[r] = fmaf(es[r][p], vv, acc[r]);
         }
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* 
     }
     // the last chunk CTA of this KV head merges every chunk's partials
     __syncthreads();
-    const int nc = (seq + kAttnChunk - 1) / kAttnChunk;
+    const int nc = (seq + kDecChunk - 1) / kDecChunk;
     if (threadIdx.x == 0) {
         __threadfence();
         s_last = atomicAdd(&counters[kvh], 1) == nc - 1;

@@ -27,10 +27,11 @@ class Engine:
         h = ctypes.c_void_p()
         _lib.check(self.lib.cllm_cuda_engine_create(gguf_path.encode(), ctx_limit, ctypes.byref(h)))
         self.h = h
-        v = (ctypes.c_int * 10)()
-        _lib.check(self.lib.cllm_cuda_engine_config(h, v, 10))
+        v = (ctypes.c_int * 11)()
+        _lib.check(self.lib.cllm_cuda_engine_config(h, v, 11))
         (self.n_layers, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff, self.vocab,
          self.n_ctx, self.launches_per_step) = (int(x) for x in v[:9])
+        self.fused = bool(v[10])
 
     def forward(self, token: int, logits: bool = True):
         """forward(token): (logits or None, greedy next token)."""

@@ -57,9 +57,10 @@ class LlamaShape:
 # BASELINE config 4 (Llama-3-8B shapes) and config 5 (Llama-3-70B shapes)
 LLAMA3_8B = LlamaShape(32, 4096, 32, 8, 14336, 128256, 4096)
 LLAMA3_70B = LlamaShape(80, 8192, 64, 8, 28672, 128256, 4096)
-# A reduced model for the token-parity tests: the 8B proportions at a size the
-# reference CPU engine runs in seconds.
-SMALL = LlamaShape(4, 2048, 16, 4, 5632, 32000, 1024)
+# A reduced model for the engine tests: the 8B proportions at a size the
+# reference CPU engine runs in seconds (n_ff a multiple of 2048, so the Q6_K
+# down-projection rows are 16-byte multiples and the fused decode step applies).
+SMALL = LlamaShape(4, 2048, 16, 4, 6144, 32000, 1024)
 
 
 def tensor_plan(cfg: LlamaShape, down_type: int = synth.Q6_K):

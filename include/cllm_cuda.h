@@ -273,8 +273,12 @@ int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int w
 int cllm_cuda_engine_create(const char* gguf_path, int ctx_limit, void** engine);
 int cllm_cuda_engine_destroy(void* engine);
 
-/* values[0..9]: n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab,
- * n_ctx, kernel launches of one decode step (graph nodes), seq_len. */
+/* values[0..10]: n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab,
+ * n_ctx, kernel launches of one decode step (graph nodes), seq_len, 1 if the
+ * decode step runs fused (RMSNorm and SwiGLU inside the GEMVs' activation
+ * quantization, one attention kernel per layer, q|k|v and gate|up as one GEMV
+ * each where the file stores them back to back; needs every decode matrix on
+ * the bulk-copy GEMV, i.e. 16-byte-multiple rows). */
 int cllm_cuda_engine_config(const void* engine, int* values, int n);
 
 /* TransformerEngine::forward(token) (engine.cpp:466-518): logits (host,
