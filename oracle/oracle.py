@@ -270,7 +270,7 @@ class ReferenceEngine:
         lib.ref_engine_config.argtypes = [_P, _P]
         lib.ref_engine_prefill.argtypes = [_P, _P, ctypes.c_int, _P, _P]
         lib.ref_engine_forward.argtypes = [_P, ctypes.c_int, _P, _P]
-        lib.ref_engine_greedy.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P]
+        lib.ref_engine_greedy.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P]
         lib.ref_engine_reset.argtypes = [_P]
         lib.ref_engine_seq_len.argtypes = [_P]
         self.lib = lib
@@ -300,13 +300,15 @@ class ReferenceEngine:
         self._check(self.lib.ref_engine_forward(self.h, int(token), _ptr(logits), ctypes.byref(nxt)))
         return logits
 
-    def greedy(self, prompt, steps: int):
-        """(tokens, top-1 minus top-2 margins) of greedy decoding after prefill(prompt)."""
+    def greedy(self, prompt, steps: int, with_scales: bool = False):
+        """(tokens, top-1 minus top-2 margins[, largest |logit|]) of greedy decoding after prefill(prompt)."""
         ids = np.ascontiguousarray(prompt, np.int32)
         toks = np.empty(steps, np.int32)
         margins = np.empty(steps, np.float32)
-        self._check(self.lib.ref_engine_greedy(self.h, _ptr(ids), len(ids), steps, _ptr(toks), _ptr(margins)))
-        return toks, margins
+        scales = np.empty(steps, np.float32)
+        self._check(self.lib.ref_engine_greedy(self.h, _ptr(ids), len(ids), steps, _ptr(toks), _ptr(margins),
+                                               _ptr(scales)))
+        return (toks, margins, scales) if with_scales else (toks, margins)
 
     def reset(self) -> None:
         self._check(self.lib.ref_engine_reset(self.h))

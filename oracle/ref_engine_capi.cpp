@@ -98,8 +98,9 @@ int ref_engine_forward(void* h, int token, float* logits, int* next) {
 // Greedy generation: prefill(prompt), then `steps` forward calls, each fed the
 // previous argmax.  tokens_out[steps] receives the generated ids (the first is
 // the prefill's argmax); margins_out (may be NULL) the top-1 minus top-2 logit
-// of each generated token.
-int ref_engine_greedy(void* h, const int* prompt, int n_prompt, int steps, int* tokens_out, float* margins_out) {
+// of each generated token, scales_out (may be NULL) the largest |logit|.
+int ref_engine_greedy(void* h, const int* prompt, int n_prompt, int steps, int* tokens_out, float* margins_out,
+                      float* scales_out) {
     return guarded([&] {
         auto* e = static_cast<RefEngine*>(h);
         std::vector<int> ids(prompt, prompt + n_prompt);
@@ -112,6 +113,11 @@ int ref_engine_greedy(void* h, const int* prompt, int n_prompt, int steps, int* 
                 for (size_t i = 0; i < logits.size(); ++i)
                     if ((int)i != tok && logits[i] > top2) top2 = logits[i];
                 margins_out[s] = top1 - top2;
+            }
+            if (scales_out) {
+                float m = 0.0f;
+                for (float v : logits) m = std::max(m, std::fabs(v));
+                scales_out[s] = m;
             }
             if (s + 1 < steps) logits = e->engine->forward(tok, true);
         }

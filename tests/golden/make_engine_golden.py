@@ -37,9 +37,10 @@ def main():
         eng = ReferenceEngine(path)
         for name, prompt in PROMPTS.items():
             eng.reset()
-            toks, margins = eng.greedy(prompt, STEPS)
+            toks, margins, scales = eng.greedy(prompt, STEPS, with_scales=True)
             out["cases"][name] = {"prompt": prompt, "tokens": [int(t) for t in toks],
-                                  "margins": [round(float(m), 4) for m in margins]}
+                                  "margins": [round(float(m), 5) for m in margins],
+                                  "scales": [round(float(m), 4) for m in scales]}
             print(name, "min margin", float(np.min(margins)), "distinct tokens", len(set(toks.tolist())))
         eng.close()
     with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "engine_greedy.json"), "w") as f:

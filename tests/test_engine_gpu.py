@@ -185,10 +185,11 @@ def test_generate_equals_host_driven_loop(engine, small_model):
     assert np.all(margins >= 0)
 
 
-def test_greedy_agreement_with_reference_is_reported(engine, small_model):
-    """Free-running greedy decoding agrees with the reference's committed
-    sequences (tests/golden/engine_greedy.json) until the two runs' re-quantization
-    noise first decides a token differently; agreement of the first steps is required."""
+def test_greedy_agreement_with_reference(engine, small_model):
+    """Free-running greedy decoding against the reference's committed sequences
+    (tests/golden/engine_greedy.json): identical until the first step whose
+    reference top-2 margin lies inside the re-quantization noise band -- the
+    two runs may decide such a step differently, and the sequences then part."""
     path, g = small_model
     for case in ("short", "long"):
         c = g["cases"][case]
@@ -197,7 +198,9 @@ def test_greedy_agreement_with_reference_is_reported(engine, small_model):
         want = np.array(c["tokens"])
         same = int(np.argmax(toks != want)) if np.any(toks != want) else len(want)
         print(f"{case}: {same} of {len(want)} greedy tokens identical")
-        assert same >= 4, f"{case}: diverged at step {same}"
+        if same < len(want):
+            margin, scale = c["margins"][same], c["scales"][same]
+            assert margin <= NOISE_BAND * scale, (case, same, margin, scale)
 
 
 def test_prefix_reuse_and_truncation(engine, small_model):
@@ -213,9 +216,11 @@ def test_prefix_reuse_and_truncation(engine, small_model):
     l_fresh, t_fresh = engine.prefill(a + b)
     assert t_reuse == t_fresh
     assert np.max(np.abs(l_reuse - l_fresh)) <= LOGIT_TOL * float(np.max(np.abs(l_fresh)))
-    l_again, _ = engine.prefill(a + b)  # the whole prompt is cached: only its last token re-runs
+    # the whole prompt cached: only its last token re-runs, through the decode
+    # step's kernels instead of the prefill's, so the bar is the noise band
+    l_again, _ = engine.prefill(a + b)
     assert engine.seq_len() == len(a) + len(b)
-    assert np.max(np.abs(l_again - l_fresh)) <= LOGIT_TOL * float(np.max(np.abs(l_fresh)))
+    assert np.max(np.abs(l_again - l_fresh)) <= NOISE_BAND * float(np.max(np.abs(l_fresh)))
 
 
 def test_context_limit_and_errors(cuda, small_model):
