@@ -43,7 +43,7 @@ def _sources(*dirs):
 def _digest(deps):
     h = hashlib.sha256()
     for d in sorted(deps):
-        h.update(d.encode())
+        h.update(os.path.relpath(d, ROOT).encode())  # the repository may live elsewhere on another machine
         with open(d, "rb") as f:
             h.update(f.read())
     return h.hexdigest()
