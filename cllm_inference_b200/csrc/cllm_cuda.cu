@@ -266,8 +266,7 @@ int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas
     return CLLM_OK;
 }
 
-constexpr uint32_t kSmemPerCta = 110 * 1024;   // two CTAs per SM
-constexpr uint32_t kSmemPerCta1 = 73 * 1024;   // one activation row: three CTAs per SM
+constexpr uint32_t kSmemPerCta = 110 * 1024;  // two CTAs per SM
 constexpr uint32_t kTileTarget = 32 * 1024;   // bytes of weights per tile
 constexpr uint32_t kFusedActMax = 48 * 1024;  // largest quantized activation kept in shared memory (M=1, K <= 32768)
 
@@ -302,13 +301,12 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
              fixed + 2ull * pl.stage_bytes <= limit;
     if (!pl.tma) pl.fused = false;
     if (pl.tma) {
-        const size_t cap = m == 1 ? kSmemPerCta1 : kSmemPerCta;
-        const size_t budget = std::max<size_t>(cap, fixed + 2ull * pl.stage_bytes);
+        const size_t budget = std::max<size_t>(kSmemPerCta, fixed + 2ull * pl.stage_bytes);
         int S = (int)std::min<size_t>(8, (budget - fixed) / pl.stage_bytes);
         if (S < 2) S = 2;
         pl.stages = S;
         pl.smem = fixed + (size_t)S * pl.stage_bytes;
-        const int per_sm = pl.smem <= cap ? di.gemv_ctas_per_sm : 1;
+        const int per_sm = pl.smem <= kSmemPerCta ? di.gemv_ctas_per_sm : 1;
         pl.grid = std::min(pl.num_tiles, per_sm * di.sms);
         // With few tiles per CTA, as few CTAs as keep the same number of tile
         // rounds: every CTA then gets the same number of tiles (within one),

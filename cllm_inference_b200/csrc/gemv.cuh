@@ -1040,15 +1040,8 @@ __host__ __device__ inline uint32_t fused_act_bytes(int M, int K) {
 // A row split over wpr > 1 warps is summed by the last of its warps to finish
 // (a shared counter per stage and row), in warp order, so the result does not
 // depend on timing.
-// Resident CTAs per SM the register budget is sized for: three for one
-// activation row (a call's grid uses two per SM, so the next call's CTAs can
-// become resident and start streaming weights while this one runs), two
-// otherwise.
-template <int M>
-constexpr int gemv_min_blocks() { return M == 1 ? 3 : 2; }
-
 template <int TYPE, int M, bool EMIT, bool FUSED>
-__global__ void __launch_bounds__(kTmaThreads, gemv_min_blocks<M>()) gemv_tma_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_addr(smem);
