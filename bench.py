@@ -84,6 +84,15 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 tensor peak (burst) in TFLOP/s and where it comes from."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
 
@@ -857,21 +866,30 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
     out["per_shape_gbs"] = per
 
     phase("prefill GEMM")
-    # prefill: matmul_quant_batch 14336x4096 Q4_K
-    pre = {}
-    w = weights[(0, "gate")]
-    for M in (64, 512, 2048):
-        x = torch.from_numpy(synth.make_activations(M, 4096, M)).to(dev)
-        y = torch.empty(M * 14336, dtype=torch.float32, device=dev)
+    # prefill: matmul_quant_batch on the tcgen05 GEMMs -- config 3 (Q4_K 14336x4096)
+    # and the FFN down projection as Q6_K (4096x14336); roofline against the
+    # measured dense bf16 burst peak (kind::f16 runs at the bf16 rate)
+    tc_peak = tensor_peak()
+    w6 = synth.make_weights_torch(synth.Q6_K, 4096, 14336, seed=606, device=dev)
+    for (key, t, w, k, n) in (("prefill_14336x4096_q4k", synth.Q4_K, weights[(0, "gate")], 4096, 14336),
+                              ("prefill_4096x14336_q6k", synth.Q6_K, w6, 14336, 4096)):
+        pre = {}
+        for M in (64, 512, 2048):
+            x = torch.from_numpy(synth.make_activations(M, k, M)).to(dev)
+            y = torch.empty(M * n, dtype=torch.float32, device=dev)
 
-        def go():
-            _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
-                                                  synth.Q4_K, None, 4096, 14336, M, ctypes.c_void_p(y.data_ptr()),
-                                                  0, cur()))
-        ms = timed(go)
-        pre[f"M={M}"] = {"ms": round(ms, 3), "tok_s": round(M / (ms * 1e-3), 1),
-                         "tops": round(2.0 * M * 14336 * 4096 / (ms * 1e-3) / 1e12, 2)}
-    out["prefill_14336x4096_q4k"] = pre
+            def go():
+                _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                                      t, None, k, n, M, ctypes.c_void_p(y.data_ptr()), 0, cur()))
+            ms = timed(go)
+            tops = 2.0 * M * n * k / (ms * 1e-3) / 1e12
+            pre[f"M={M}"] = {"ms": round(ms, 3), "tok_s": round(M / (ms * 1e-3), 1), "tops": round(tops, 2),
+                             "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": tc_peak[0],
+                                          "unit": "TFLOP/s", "frac": round(tops / tc_peak[0], 4),
+                                          "peak_source": tc_peak[1]}}
+            del x, y
+        out[key] = pre
+    del w6
 
     phase("end-to-end sweep through host buffers")
     # e2e: the same sweep through the host-buffer C ABI call

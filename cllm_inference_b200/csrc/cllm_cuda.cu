@@ -25,6 +25,7 @@
 #include "dequant.cuh"
 #include "fallback.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc_q6k.cuh"
 #include "gemv.cuh"
 #include "shard.cuh"
 #include "quantize.cuh"
@@ -410,13 +411,14 @@ int encode_fn(EncodeTiledFn* out) {
     return CLLM_OK;
 }
 
-// 2-D tiled tensor map over a row-major [rows][cols] array.
+// 2-D tiled tensor map over a row-major [rows][cols] array (row pitch in bytes,
+// 0 = dense).
 int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t cols,
-                uint64_t rows, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+                uint64_t rows, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz, uint64_t pitch = 0) {
     EncodeTiledFn enc;
     if (int rc = encode_fn(&enc)) return rc;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * (uint64_t)esize};
+    const cuuint64_t strides[1] = {pitch ? pitch : cols * (uint64_t)esize};
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -427,20 +429,59 @@ int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void*
 }
 
 bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_rows) {
-    return type == kQ4_K && n_rows >= kTcMinRows && K >= 256 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+    return (type == kQ4_K || type == kQ6_K) && n_rows >= kTcMinRows && K >= 256 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
            (row_bytes & 15) == 0;
 }
 
-// Workspace bytes of the prefill activations (fp16 q_x, dx, dx*bsum) for M rows of K.
-size_t prefill_bytes(int M, int K) {
+// Tokens per row of the Q6_K block-major dx array (16-byte rows for its tensor map).
+inline int64_t q6_dx_pitch(int M) { return ((int64_t)M + 3) & ~int64_t(3); }
+
+// Workspace bytes of the prefill activations for M rows of K: fp16 q_x, then
+// (dx, dx*bsum) [M][nb] for Q4_K, or dx [nb][pitch] and the -128 flags [M][nb] for Q6_K.
+size_t prefill_bytes(int type, int M, int K) {
     const size_t nb = (size_t)K / 32;
+    if (type == kQ6_K)
+        return align256((size_t)M * K * 2) + align256(nb * (size_t)q6_dx_pitch(M) * 4) + align256((size_t)M * nb);
     return align256((size_t)M * K * 2) + align256((size_t)M * nb * 8);
 }
 
-// y[M][N] = batch matmul through prefill_q4k_kernel; x, w, bias, y on the device,
-// ws = prefill_bytes(M, K) of workspace.
-int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const float* bias, int K, int N, int M,
-                   float* y, uint8_t* ws, int dev, cudaStream_t st) {
+// Q6_K: y[M][N] through prefill_q6k_kernel and the sign-trick fix-up.
+int launch_prefill_q6k(const float* x, const uint8_t* w, int64_t row_bytes, const float* bias, int K, int N, int M,
+                       float* y, uint8_t* ws, int dev, cudaStream_t st) {
+    const DeviceInfo& di = g_dev[dev];
+    const int64_t nb = K / 32, mp = q6_dx_pitch(M);
+    __half* a16 = reinterpret_cast<__half*>(ws);
+    float* dxT = reinterpret_cast<float*>(ws + align256((size_t)M * K * 2));
+    uint8_t* flags = ws + align256((size_t)M * K * 2) + align256((size_t)(nb * mp * 4));
+    const int64_t blocks = (int64_t)M * nb;
+    const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
+    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, nullptr, dxT, mp, flags);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    CUtensorMap map_x, map_w, map_dx;
+    if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxT, (uint64_t)M, (uint64_t)nb, kTcBM, 8,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, (uint64_t)mp * 4))
+        return rc;
+    if (int rc = make_map_2d(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, (uint64_t)K, (uint64_t)M, kTcBK, kTcBM,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    if (int rc = make_map_2d(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, (uint64_t)row_bytes, (uint64_t)N, kQ6RawRow,
+                             kTcBN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+    if (int rc = opt_in_smem(reinterpret_cast<const void*>(prefill_q6k_kernel), dev)) return rc;
+    const Q6Params qp{M, N, K, bias, y};
+    const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
+    prefill_q6k_kernel<<<tgrid, kTcThreads, kQ6SmemBytes, st>>>(map_x, map_w, map_dx, qp);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    prefill_q6k_fixup_kernel<<<(unsigned)M, 128, 0, st>>>(w, row_bytes, a16, dxT, mp, flags, K, N, y);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
+// y[M][N] = batch matmul through the tcgen05 kernel of the weight type; x, w,
+// bias, y on the device, ws = prefill_bytes(type, M, K) of workspace.
+int launch_prefill(int type, const float* x, const uint8_t* w, int64_t row_bytes, const float* bias, int K, int N,
+                   int M, float* y, uint8_t* ws, int dev, cudaStream_t st) {
+    if (type == kQ6_K) return launch_prefill_q6k(x, w, row_bytes, bias, K, N, M, y, ws, dev, st);
     const DeviceInfo& di = g_dev[dev];
     const size_t nb = (size_t)K / 32;
     const size_t off_a = 0, off_dx = align256((size_t)M * K * 2);
@@ -448,7 +489,7 @@ int launch_prefill(const float* x, const uint8_t* w, int64_t row_bytes, const fl
     float* dxx = reinterpret_cast<float*>(ws + off_dx);  // [M][2*nb]: (dx, dx*bsum)
     const int64_t blocks = (int64_t)M * (K / 32);
     const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
-    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx);
+    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, nullptr, 0, nullptr);
     CLLM_CUDA_TRY(cudaGetLastError());
     CUtensorMap map_a, map_w, map_dx;
     if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxx, (uint64_t)(2 * nb), (uint64_t)M, 16, kTcBM,
@@ -643,7 +684,7 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
         total = align256(total + (size_t)n_rows * out_dim * 4);
     }
     const size_t off_pre = total;
-    if (use_tc) total += prefill_bytes(n_rows, in_dim);
+    if (use_tc) total += prefill_bytes(type, n_rows, in_dim);
     const size_t off_img = total;
     const bool want_image = !use_tc && !fallback && in_dim >= kImageMinK;
     if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
@@ -674,7 +715,7 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
     if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
 
     if (use_tc) {
-        if (int rc = launch_prefill(xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
+        if (int rc = launch_prefill(type, xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
             return rc;
     }
     if (pre.op != kPreNone && (use_tc || fallback || (flags & CLLM_X_HOST)))
@@ -986,14 +1027,15 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
     int vals[8] = {chunks * (pl.fused ? 1 : 2), pl.tma, pl.fused, pl.rows_per_tile, pl.wpr,
                    pl.stages, pl.grid, (int)pl.smem};
     if (prefill_eligible(type, w, row_bytes, in_dim, n_rows)) {
-        vals[0] = 2;  // activation preparation + the tcgen05 GEMM
+        // activation preparation + the tcgen05 GEMM (+ the Q6_K sign-trick fix-up)
+        vals[0] = type == kQ6_K ? 3 : 2;
         vals[1] = 2;
         vals[2] = 0;
         vals[3] = kTcBN;
         vals[4] = 0;
         vals[5] = kTcStA;
         vals[6] = ((n_rows + kTcBM - 1) / kTcBM) * ((out_dim + kTcBN - 1) / kTcBN);
-        vals[7] = (int)kTcSmemBytes;
+        vals[7] = (int)(type == kQ6_K ? kQ6SmemBytes : kTcSmemBytes);
     }
     for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];
     return CLLM_OK;

@@ -567,11 +567,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // Prefill activation preparation: quantize_row_q8_0 per 32-value block
-// (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16 and the pairs
-// (dx, dx*bsum) per block.
+// (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16 and, where the
+// pointers are given, the pairs (dx, dx*bsum) per block [M][2*nb] (Q4_K), dx
+// block-major [nb][mp] (Q6_K) and a flag per block that holds a -128 (Q6_K).
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ x, int64_t n,
                                                            int64_t total_blocks, __half* __restrict__ a16,
-                                                           float* __restrict__ dxx) {
+                                                           float* __restrict__ dxx, float* __restrict__ dxT,
+                                                           int64_t mp, uint8_t* __restrict__ flags) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int64_t nb = n >> 5;
@@ -592,9 +594,14 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
         int s = q;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if (lane == 0) {  // (dx, dx*bsum) pairs, [M][2*nb]
+        if (lane == 0 && dxx) {  // (dx, dx*bsum) pairs, [M][2*nb]
             dxx[2 * (r * nb + b)] = d;
             dxx[2 * (r * nb + b) + 1] = d * (float)s;
+        }
+        if (lane == 0 && dxT) dxT[b * mp + r] = d;
+        if (flags) {
+            const unsigned neg = __ballot_sync(0xFFFFFFFFu, q == -128);
+            if (lane == 0) flags[r * nb + b] = neg ? 1 : 0;
         }
     }
 }

@@ -78,3 +78,63 @@ def test_prefill_config3_exact_shape(cuda, lib, oracle, m):
     yo, ab = oracle.matmul(x[toks], G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows),
                            with_abs=True)
     G.assert_rows_close(y[np.ix_(toks, rows)], yo, ab, REL_TOL, f"config 3 M={m}")
+
+
+# Q6_K: K a multiple of 2048 keeps its 210-byte-per-super-block rows 16-byte
+# multiples (the tensor map's row pitch); the full int8 scale range makes
+# sc * (q6 - 32) exceed fp16's exact integers, which the kernel must not need.
+Q6_SHAPES = [(2048, 128, 64), (2048, 200, 100), (4096, 300, 129), (4096, 256, 257), (6144, 136, 192)]
+
+
+@pytest.mark.parametrize("k,n,m", Q6_SHAPES)
+def test_prefill_q6k_tcgen05(cuda, lib, oracle, k, n, m):
+    t = synth.Q6_K
+    w = synth.make_weights(t, n, k, seed=k + n + m, q6_scale_max=128)
+    x = synth.make_activations(m, k, seed=m + 7)
+    bias = np.linspace(-2, 2, n, dtype=np.float32) if m % 2 else None
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2, "expected the tcgen05 path"
+    y = G.matmul(lib, x, w, t, k, n, bias=bias)
+    yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
+    G.assert_rows_close(y, yo, ab, REL_TOL, f"Q6_K prefill {k}x{n} m={m}")
+
+
+def test_prefill_q6k_nan_tokens(cuda, lib, oracle):
+    """Tokens with NaN inputs: the NaN quantizes to -128 and the AVX2 sign
+    trick turns -128 * w (w < 0) into 128 * w; the fix-up kernel must
+    reproduce it.  Tokens with one NaN, a NaN in every block, and all-NaN."""
+    t, k, n, m = synth.Q6_K, 2048, 256, 96
+    w = synth.make_weights(t, n, k, seed=5, q6_scale_max=128)
+    x = synth.make_activations(m, k, seed=6)
+    x[3, 17] = np.nan
+    x[40, ::32] = np.nan
+    x[41, 5::32] = np.nan
+    x[95, :] = np.nan
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2
+    y = G.matmul(lib, x, w, t, k, n)
+    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+    assert np.isfinite(yo[[3, 40, 41, 95]]).all()
+    G.assert_rows_close(y, yo, ab, REL_TOL, "Q6_K prefill, NaN tokens")
+
+
+def test_prefill_q6k_ineligible_rows_take_gemv(cuda, lib):
+    """K = 1024 gives 840-byte rows (not 16-byte multiples): the plan keeps the GEMV path."""
+    t, k, n, m = synth.Q6_K, 1024, 64, 128
+    w = synth.make_weights(t, n, k, seed=1)
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] != 2
+
+
+def test_prefill_q6k_config3_down_shape(cuda, lib, oracle):
+    """The config-3 FFN down projection as Q6_K (4096 rows x 14336 in) at
+    M = 512 on the tcgen05 GEMM: three rows per 128-row tile, every token."""
+    t, k, n, m = synth.Q6_K, 14336, 4096, 512
+    w = synth.make_weights(t, n, k, seed=4242, q6_scale_max=128)
+    x = synth.make_activations(m, k, seed=77)
+    _, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2, "expected the tcgen05 path"
+    y = G.matmul(lib, x, w, t, k, n)
+    rows = _tile_samples(n, 128, np.random.default_rng(9))
+    yo, ab = oracle.matmul(x, G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows), with_abs=True)
+    G.assert_rows_close(y[:, rows], yo, ab, REL_TOL, "config 3 down as Q6_K, M=512")
