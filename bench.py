@@ -916,7 +916,9 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
     step_bytes = sum(call_bytes(t, k, n, 1) for (_, _, t, k, n) in calls)
     out["e2e"] = {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                   "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
-                  "api": "cllm_cuda_matmul_quant(..., CLLM_HOST_IO) per projection, pinned host x/y"}
+                  "api": "cllm_cuda_matmul_quant(..., CLLM_HOST_IO) per projection, pinned host x/y (x read in place "
+                         "by the quantization kernel, y <= 16 KB written in place, larger y copied out; each "
+                         "call's operations replayed from a graph cached per argument tuple)"}
     return out
 
 

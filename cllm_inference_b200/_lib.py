@@ -28,6 +28,7 @@ ERR_TOO_LARGE = -8
 X_HOST, Y_HOST, W_HOST = 1, 2, 4
 SHARD_WAIT_PREV = 1
 SHARD_PAD_WORDS = 16
+IPC_HANDLE_BYTES = 64
 HOST_IO = X_HOST | Y_HOST
 
 _P = ctypes.c_void_p
@@ -59,6 +60,10 @@ SIGNATURES = {
                                              ctypes.POINTER(_P), _P, _U, _P]),
     "cllm_cuda_shard_wait": (_I, [_P, _P, _I, _P]),
     "cllm_cuda_shard_barrier": (_I, [ctypes.POINTER(_P), _P, _I, _I, _P]),
+    "cllm_cuda_ipc_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(_P), _P]),
+    "cllm_cuda_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "cllm_cuda_ipc_close": (_I, [_P]),
+    "cllm_cuda_ipc_free": (_I, [_P]),
     "cllm_cuda_engine_create": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
     "cllm_cuda_engine_destroy": (_I, [_P]),
     "cllm_cuda_engine_config": (_I, [_P, ctypes.POINTER(ctypes.c_int), _I]),

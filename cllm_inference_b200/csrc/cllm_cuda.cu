@@ -15,7 +15,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <map>
+#include <unordered_map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -84,6 +86,10 @@ struct DeviceInfo {
     // CTAs become resident while this one runs (programmatic dependent
     // launch) and prefetch their first weight tiles.
     int gemv_ctas_per_sm = 2;
+    // Host I/O of the GEMV path through mapped pinned memory instead of copy
+    // operations: bit 0 reads x in place, bit 1 writes y in place (environment
+    // CLLM_HOSTIO_DIRECT, 0..3).
+    int hostio_direct = 3;
 };
 
 std::mutex g_mu;
@@ -95,6 +101,9 @@ struct Workspace {
 };
 Workspace g_ws[64];
 std::mutex g_ws_mu[64];  // one per device: held from workspace() until the call's kernels are enqueued
+// Bumped whenever device memory a cached host-I/O graph may point at moves:
+// the workspace is reallocated, or a weight range is registered or removed.
+std::atomic<uint64_t> g_memory_gen{0};
 
 struct WeightRange {
     size_t bytes;
@@ -124,10 +133,22 @@ int ensure_device(int* out_dev) {
         di.sms = prop.multiProcessorCount;
         di.max_smem_optin = prop.sharedMemPerBlockOptin;
         if (const char* v = std::getenv("CLLM_GEMV_CTAS_PER_SM")) di.gemv_ctas_per_sm = std::atoi(v) == 1 ? 1 : 2;
+        if (const char* v = std::getenv("CLLM_HOSTIO_DIRECT")) di.hostio_direct = std::atoi(v) & 3;
         di.ready = true;
     }
     *out_dev = dev;
     return CLLM_OK;
+}
+
+// Device address of pinned host memory the GPU can address in place
+// (cudaHostAlloc, cudaMallocHost, cudaHostRegister), else nullptr.
+void* mapped_host(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
 }
 
 // Grow the device workspace to at least `bytes` (never shrinks).  Takes the
@@ -149,6 +170,7 @@ int workspace(int dev, size_t bytes, uint8_t** out, std::unique_lock<std::mutex>
         const size_t cap = std::max<size_t>(bytes + (bytes >> 2), size_t(4) << 20);
         CLLM_CUDA_TRY(cudaMalloc(&ws.ptr, cap));
         ws.cap = cap;
+        g_memory_gen.fetch_add(1);
     }
     *out = static_cast<uint8_t*>(ws.ptr);
     return CLLM_OK;
@@ -633,6 +655,13 @@ int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, 
     }
     return CLLM_OK;
 }
+// Internal flag of matmul_quant_impl: enqueue everything, but leave the final
+// stream synchronization of a host-y call to the caller (graph capture).
+constexpr unsigned kNoSync = 1u << 30;
+// Largest y written in place to mapped host memory: the GEMV stores single
+// floats, so beyond this a copy-engine transfer of y is the faster way out.
+constexpr size_t kDirectYBytes = 16 * 1024;
+
 // matmul_quant / matmul_quant_batch (quant.cpp:1374-1475) behind
 // cllm_cuda_matmul_quant.  Scratch: the device workspace (scratch == nullptr),
 // or a caller-owned buffer of scratch_cap bytes (the engine's decode step,
@@ -643,7 +672,7 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
                       size_t* need, PreOp pre = PreOp{kPreNone, nullptr, 0.0f}) {
     const char* fname = n_rows > 1 ? "matmul_quant_batch" : "matmul_quant";
     if (n_rows <= 0) return CLLM_OK;  // quant.cpp:1436
-    if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))
+    if (flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST | kNoSync))
         return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
     if (in_dim < 0 || out_dim < 0) return fail(CLLM_ERR_INVALID_ARG, "%s: negative dimension", fname);
     const int bsz = block_size_of(type);
@@ -670,23 +699,35 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
     }
 
     const bool use_tc = !fallback && prefill_eligible(type, wd, row_bytes, in_dim, n_rows);
+    const bool gemv_path = !use_tc && !fallback;
+    // GEMV host I/O without copy operations where the host buffers are pinned
+    // and mapped: x is then read once, by the quantization kernel, and y is
+    // written by the GEMV's own stores.
+    const float* x_map = nullptr;
+    float* y_map = nullptr;
+    if (gemv_path) {
+        if ((flags & CLLM_X_HOST) && (di.hostio_direct & 1)) x_map = static_cast<const float*>(mapped_host(x));
+        if ((flags & CLLM_Y_HOST) && (di.hostio_direct & 2) && (size_t)n_rows * out_dim * 4 <= kDirectYBytes)
+            y_map = static_cast<float*>(mapped_host(y));
+    }
     const int mchunk = std::min(n_rows, 8);
     const ActLayout L = act_layout(use_tc || fallback ? 0 : mchunk, in_dim, 0);
     size_t off_x = L.end, off_b = L.end, off_y = L.end, total = L.end;
     if (flags & CLLM_X_HOST) {
         off_x = total;
-        total = align256(total + (size_t)n_rows * in_dim * 4);
+        if (!x_map) total = align256(total + (size_t)n_rows * in_dim * 4);
         off_b = total;
         if (bias) total = align256(total + (size_t)out_dim * 4);
     }
-    if (flags & CLLM_Y_HOST) {
+    if ((flags & CLLM_Y_HOST) && !y_map) {
         off_y = total;
         total = align256(total + (size_t)n_rows * out_dim * 4);
     }
     const size_t off_pre = total;
     if (use_tc) total += prefill_bytes(type, n_rows, in_dim);
     const size_t off_img = total;
-    const bool want_image = !use_tc && !fallback && in_dim >= kImageMinK;
+    // a mapped x goes through the activation image so that it crosses the host link once
+    const bool want_image = gemv_path && (in_dim >= kImageMinK || x_map);
     if (want_image) total = align256(total + image_bytes(mchunk, in_dim));
     if (need) {
         *need = total;
@@ -705,14 +746,18 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
     const float* bd = bias;
     float* yd = y;
     if (flags & CLLM_X_HOST) {
-        xd = reinterpret_cast<float*>(ws + off_x);
-        CLLM_CUDA_TRY(cudaMemcpyAsync((void*)xd, x, (size_t)n_rows * in_dim * 4, cudaMemcpyHostToDevice, st));
+        if (x_map) {
+            xd = x_map;
+        } else {
+            xd = reinterpret_cast<float*>(ws + off_x);
+            CLLM_CUDA_TRY(cudaMemcpyAsync((void*)xd, x, (size_t)n_rows * in_dim * 4, cudaMemcpyHostToDevice, st));
+        }
         if (bias) {
             bd = reinterpret_cast<float*>(ws + off_b);
             CLLM_CUDA_TRY(cudaMemcpyAsync((void*)bd, bias, (size_t)out_dim * 4, cudaMemcpyHostToDevice, st));
         }
     }
-    if (flags & CLLM_Y_HOST) yd = reinterpret_cast<float*>(ws + off_y);
+    if (flags & CLLM_Y_HOST) yd = y_map ? y_map : reinterpret_cast<float*>(ws + off_y);
 
     if (use_tc) {
         if (int rc = launch_prefill(type, xd, wd, row_bytes, bd, in_dim, out_dim, n_rows, yd, ws + off_pre, dev, st))
@@ -728,9 +773,126 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
             return rc;
     }
     if (flags & CLLM_Y_HOST) {
-        CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
-        CLLM_CUDA_TRY(cudaStreamSynchronize(st));
+        if (!y_map) CLLM_CUDA_TRY(cudaMemcpyAsync(y, yd, (size_t)n_rows * out_dim * 4, cudaMemcpyDeviceToHost, st));
+        if (!(flags & kNoSync)) CLLM_CUDA_TRY(cudaStreamSynchronize(st));
     }
+    return CLLM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Host-I/O calls as cached CUDA graphs.  A matmul_quant call with host x / y
+// is several stream operations (copy in, quantization, GEMV, copy out) whose
+// launch costs dominate a decode-sized call.  When every host buffer is
+// pinned, the call's operations are captured once per argument tuple into a
+// graph, and later calls with the same pointers and shape replay it: one
+// launch and one synchronization.  Graphs read their buffers when they run,
+// so new contents of x and of the weights are seen; a graph is rebuilt when
+// device memory it points at has moved (g_memory_gen).
+struct HostCallKey {
+    const void *x, *w, *bias;
+    void* y;
+    int type, in_dim, out_dim, n_rows;
+    unsigned flags;
+    bool operator==(const HostCallKey& o) const {
+        return x == o.x && w == o.w && bias == o.bias && y == o.y && type == o.type && in_dim == o.in_dim &&
+               out_dim == o.out_dim && n_rows == o.n_rows && flags == o.flags;
+    }
+};
+struct HostCallHash {
+    size_t operator()(const HostCallKey& k) const {
+        size_t h = std::hash<const void*>()(k.x);
+        auto mix = [&h](size_t v) { h ^= v + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2); };
+        mix(std::hash<const void*>()(k.w));
+        mix(std::hash<const void*>()(k.bias));
+        mix(std::hash<const void*>()(k.y));
+        mix((size_t)k.type * 1000003u ^ (size_t)k.in_dim);
+        mix((size_t)k.out_dim * 1000033u ^ (size_t)k.n_rows ^ ((size_t)k.flags << 40));
+        return h;
+    }
+};
+struct HostCallGraph {
+    cudaGraphExec_t exec = nullptr;  // nullptr: the call runs directly (prefill path, capture refused)
+    uint64_t gen = 0;
+    size_t total = 0;  // workspace bytes the graph uses
+};
+constexpr size_t kHostGraphMax = 4096;  // cached graphs per device
+std::unordered_map<HostCallKey, HostCallGraph, HostCallHash> g_host_graphs[64];  // under g_ws_mu[dev]
+cudaStream_t g_capture_stream[64];
+
+void clear_host_graphs(int dev) {
+    for (auto& kv : g_host_graphs[dev])
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    g_host_graphs[dev].clear();
+}
+
+// The host-I/O call through a cached graph; *handled = false when the call
+// does not qualify (pageable buffers, prefill path, capture refused), in
+// which case the caller runs it directly.
+int host_graph_call(const float* x, const void* w, int type, const float* bias, int in_dim, int out_dim,
+                    int n_rows, float* y, unsigned flags, cudaStream_t st, bool* handled) {
+    *handled = false;
+    if (n_rows <= 0 || out_dim <= 0 || in_dim <= 0 || !x || !w || !y) return CLLM_OK;
+    if (((flags & CLLM_X_HOST) && (!mapped_host(x) || (bias && !mapped_host(bias)))) ||
+        ((flags & CLLM_Y_HOST) && !mapped_host(y)))
+        return CLLM_OK;
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    const HostCallKey key{x, w, bias, y, type, in_dim, out_dim, n_rows, flags};
+    auto& cache = g_host_graphs[dev];
+    std::unique_lock<std::mutex> ws_lock(g_ws_mu[dev]);  // held until the call has finished
+    auto it = cache.find(key);
+    if (it != cache.end() && it->second.gen == g_memory_gen.load() && g_ws[dev].cap >= it->second.total) {
+        if (!it->second.exec) return CLLM_OK;
+        CLLM_CUDA_TRY(cudaGraphLaunch(it->second.exec, st));
+        CLLM_CUDA_TRY(cudaStreamSynchronize(st));
+        *handled = true;
+        return CLLM_OK;
+    }
+    ws_lock.unlock();
+
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        (void)cudaGetLastError();
+        return CLLM_OK;  // the caller's own capture records the operations directly
+    }
+    if (!has_vec_dot_of(type) || in_dim % block_size_of(type) != 0) return CLLM_OK;
+    const int64_t row_bytes = (int64_t)(in_dim / block_size_of(type)) * type_size_of(type);
+    const uint8_t* wd = static_cast<const uint8_t*>(w);
+    if ((flags & CLLM_W_HOST) && lookup(w, &wd, nullptr) != CLLM_OK) return CLLM_OK;  // reported directly
+    const bool direct = prefill_eligible(type, wd, row_bytes, in_dim, n_rows);  // the tcgen05 path
+    size_t total = 0;
+    if (int rc = matmul_quant_impl(x, w, type, bias, in_dim, out_dim, n_rows, y, flags, st, nullptr, 0, &total))
+        return rc;
+    uint8_t* ws = nullptr;
+    if (int rc = workspace(dev, total, &ws, ws_lock)) return rc;  // may move the workspace (new generation)
+    const uint64_t gen = g_memory_gen.load();
+    it = cache.find(key);
+    if (it != cache.end()) {
+        if (it->second.exec) cudaGraphExecDestroy(it->second.exec);
+        cache.erase(it);
+    }
+    if (cache.size() >= kHostGraphMax) clear_host_graphs(dev);
+    if (direct) {
+        cache.emplace(key, HostCallGraph{nullptr, gen, 0});
+        return CLLM_OK;
+    }
+    if (!g_capture_stream[dev])
+        CLLM_CUDA_TRY(cudaStreamCreateWithFlags(&g_capture_stream[dev], cudaStreamNonBlocking));
+    cudaStream_t cap = g_capture_stream[dev];
+    CLLM_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeRelaxed));
+    const int rc = matmul_quant_impl(x, w, type, bias, in_dim, out_dim, n_rows, y, flags | kNoSync, cap, ws, total,
+                                     nullptr);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(cap, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (rc == CLLM_OK && ec == cudaSuccess && g && cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) exec = nullptr;
+    if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();
+    cache.emplace(key, HostCallGraph{exec, gen, total});
+    if (!exec) return CLLM_OK;  // not captured: the direct path runs the call (and reports its errors)
+    CLLM_CUDA_TRY(cudaGraphLaunch(exec, st));
+    CLLM_CUDA_TRY(cudaStreamSynchronize(st));
+    *handled = true;
     return CLLM_OK;
 }
 
@@ -808,6 +970,7 @@ int cllm_cuda_register_weights(const void* host_base, size_t bytes, void** dev_b
     {
         std::lock_guard<std::mutex> lk(g_mu);
         g_weights[h] = WeightRange{bytes, alloc, dev_ptr, dev};
+        g_memory_gen.fetch_add(1);
     }
     if (dev_base) *dev_base = dev_ptr;
     return CLLM_OK;
@@ -821,6 +984,7 @@ int cllm_cuda_unregister_weights(const void* host_base) {
         if (it == g_weights.end()) return fail(CLLM_ERR_NOT_REGISTERED, "unregister_weights: unknown range");
         alloc = it->second.alloc;
         g_weights.erase(it);
+        g_memory_gen.fetch_add(1);
     }
     CLLM_CUDA_TRY(cudaFree(alloc));
     return CLLM_OK;
@@ -849,6 +1013,13 @@ int cllm_cuda_quantize_q8_0(const float* x, int64_t n, int rows, float* scales, 
 
 int cllm_cuda_matmul_quant(const float* x, const void* w, int type, const float* bias, int in_dim,
                            int out_dim, int n_rows, float* y, unsigned flags, void* stream) {
+    if ((flags & CLLM_Y_HOST) && !(flags & ~(CLLM_X_HOST | CLLM_Y_HOST | CLLM_W_HOST))) {
+        bool handled = false;
+        if (int rc = host_graph_call(x, w, type, bias, in_dim, out_dim, n_rows, y, flags,
+                                     static_cast<cudaStream_t>(stream), &handled))
+            return rc;
+        if (handled) return CLLM_OK;
+    }
     return matmul_quant_impl(x, w, type, bias, in_dim, out_dim, n_rows, y, flags, static_cast<cudaStream_t>(stream),
                              nullptr, 0, nullptr);
 }
@@ -1209,6 +1380,49 @@ int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int wor
     int dev;
     if (int rc = ensure_device(&dev)) return rc;
     return launch_shard_kernel(shard_wait_kernel, static_cast<cudaStream_t>(stream), own_pad, epoch, world);
+}
+
+int cllm_cuda_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+    if (!bytes || !dev_ptr || !handle) return fail(CLLM_ERR_INVALID_ARG, "ipc_alloc: bad arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) == CLLM_IPC_HANDLE_BYTES, "IPC handle size");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    void* p = nullptr;
+    CLLM_CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(CLLM_ERR_CUDA, "ipc_alloc: %s", cudaGetErrorString(e));
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *dev_ptr = p;
+    return CLLM_OK;
+}
+
+int cllm_cuda_ipc_open(const void* handle, void** dev_ptr) {
+    if (!handle || !dev_ptr) return fail(CLLM_ERR_INVALID_ARG, "ipc_open: bad arguments");
+    int dev;
+    if (int rc = ensure_device(&dev)) return rc;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    CLLM_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr = p;
+    return CLLM_OK;
+}
+
+int cllm_cuda_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return fail(CLLM_ERR_INVALID_ARG, "ipc_close: null pointer");
+    CLLM_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+    return CLLM_OK;
+}
+
+int cllm_cuda_ipc_free(void* dev_ptr) {
+    if (!dev_ptr) return fail(CLLM_ERR_INVALID_ARG, "ipc_free: null pointer");
+    CLLM_CUDA_TRY(cudaFree(dev_ptr));
+    return CLLM_OK;
 }
 
 int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream) {

@@ -10,7 +10,7 @@ Two ways to gather the slices:
 
 * ``RowShardGroup.matmul`` -- the product path.  The GEMV stores each output
   element straight into the y buffer of every rank (NVLink peer mappings of
-  symmetric memory); its last warp announces the round to every rank with a
+  buffers exchanged as CUDA IPC handles, ``cllm_cuda_ipc_*``); its last warp announces the round to every rank with a
   release store, and the next call (or ``sync``) waits for all announcements
   before it reads its input (``cllm_cuda_matmul_quant_rowshard``,
   ``cllm_cuda_shard_wait``).  No separate collective runs.
@@ -79,45 +79,92 @@ class ShardedWeight:
         self.begin, self.rows = shard_rows(out_dim, world, rank)
 
 
+def open_peer_buffers(lib, nbytes: int, rank: int, world: int, allgather):
+    """Allocate this rank's peer-mapped buffer and map every other rank's.
+
+    lib: the C ABI (cllm_cuda_ipc_alloc / cllm_cuda_ipc_open); allgather:
+    bytes -> list of every rank's bytes in rank order (any host transport).
+    Returns (own pointer, [pointer of rank q's buffer in this process],
+    [pointers opened here, to close before the owners free theirs])."""
+    own = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+    _lib.check(lib.cllm_cuda_ipc_alloc(nbytes, ctypes.byref(own), handle))
+    handles = allgather(bytes(handle))
+    if len(handles) != world or bytes(handles[rank]) != bytes(handle):
+        raise RuntimeError("peer buffer exchange returned a wrong handle table")
+    ptrs, opened = [], []
+    for q, hq in enumerate(handles):
+        if q == rank:
+            ptrs.append(own.value)
+            continue
+        buf = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(hq)
+        p = ctypes.c_void_p()
+        _lib.check(lib.cllm_cuda_ipc_open(buf, ctypes.byref(p)))
+        ptrs.append(p.value)
+        opened.append(p.value)
+    return own.value, ptrs, opened
+
+
+class _DeviceArray:
+    """fp32 / int32 device memory at a raw address, for torch.as_tensor (no copy)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def _torch_allgather(group):
+    def allgather(b: bytes):
+        import torch.distributed as dist
+
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, b, group=group)
+        return out
+    return allgather
+
+
 class RowShardGroup:
-    """The GPUs of a torch.distributed group (backend nccl, one process per GPU)
-    running row-sharded matmul_quant calls.
+    """The GPUs of one node (one process per GPU) running row-sharded
+    matmul_quant calls.
 
-    max_out / max_rows size the two symmetric y buffers (double-buffered: a
-    fast rank may write call n+1's slice while a slow rank still reads call
-    n's result)."""
+    Every rank's y buffers and signal pad live in one allocation made by the
+    C ABI (cllm_cuda_ipc_alloc) and mapped into the other ranks by CUDA IPC
+    handles (plain NVLink peer mappings, no multicast objects).  The handles
+    travel over `allgather` (bytes -> list of every rank's bytes), by default
+    torch.distributed's all_gather_object on `group`.
 
-    def __init__(self, max_out: int, max_rows: int = 8, group=None):
+    max_out / max_rows size the two y buffers (double-buffered: a fast rank
+    may write call n+1's slice while a slow rank still reads call n's result)."""
+
+    def __init__(self, max_out: int, max_rows: int = 8, group=None, allgather=None, rank=None, world=None):
         import torch
         import torch.distributed as dist
 
-        # plain peer loads and stores only: no NVLink multicast objects
-        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
-        import torch.distributed._symmetric_memory as symm
-
-        self.group = group if group is not None else dist.group.WORLD
-        self.world = dist.get_world_size(self.group)
-        self.rank = dist.get_rank(self.group)
+        self.group = group if group is not None else (dist.group.WORLD if dist.is_initialized() else None)
+        self.world = world if world is not None else dist.get_world_size(self.group)
+        self.rank = rank if rank is not None else dist.get_rank(self.group)
         if self.world > 8:
             raise ValueError("row sharding is limited to the 8 GPUs of one node")
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.lib = _lib.load()
         _lib.check(self.lib.cllm_cuda_init(self.dev.index))
         self.max_out, self.max_rows = max_out, max_rows
-        gname = self.group.group_name
-        self._y = [symm.empty(max_rows * max_out, dtype=torch.float32, device=self.dev) for _ in range(2)]
-        self._sig = symm.empty(64, dtype=torch.int32, device=self.dev)
-        self._sig.zero_()
-        self._epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
-        torch.cuda.synchronize()
-        hy = [symm.rendezvous(t, gname) for t in self._y]
-        hs = symm.rendezvous(self._sig, gname)
+        ybytes = (max_rows * max_out * 4 + 255) // 256 * 256
+        self._off_sig = 2 * ybytes
+        self._off_epoch = self._off_sig + 256
+        nbytes = self._off_epoch + 256
+        self._allgather = allgather or _torch_allgather(self.group)
+        self._own, ptrs, self._opened = open_peer_buffers(self.lib, nbytes, self.rank, self.world,
+                                                          self._allgather)
         arr = ctypes.c_void_p * self.world
-        self._yptrs = [arr(*[int(p) for p in h.buffer_ptrs]) for h in hy]
-        self._sigptrs = arr(*[int(p) for p in hs.buffer_ptrs])
-        self._handles = hy + [hs]
+        self._yptrs = [arr(*[p + i * ybytes for p in ptrs]) for i in range(2)]
+        self._sigptrs = arr(*[p + self._off_sig for p in ptrs])
+        self._y = [torch.as_tensor(_DeviceArray(self._own + i * ybytes, max_rows * max_out, "<f4"), device=self.dev)
+                   for i in range(2)]
+        self._sig_ptr = self._own + self._off_sig
+        self._epoch_ptr = self._own + self._off_epoch
         self._flip = 0
-        dist.barrier(group=self.group)
+        self._allgather(b"ready")  # every rank has mapped every buffer before any call writes into it
 
     def shard(self, w_full, type_: int, in_dim: int, out_dim: int) -> ShardedWeight:
         """Copy this rank's rows of a full weight matrix (uint8 tensor, host or
@@ -154,7 +201,7 @@ class RowShardGroup:
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
             ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, sw.in_dim, sw.out_dim,
             self.rank, self.world, n_rows, self._yptrs[buf], None if solo else self._sigptrs,
-            None if solo else ctypes.c_void_p(self._epoch.data_ptr()), 0 if solo else _lib.SHARD_WAIT_PREV, st))
+            None if solo else ctypes.c_void_p(self._epoch_ptr), 0 if solo else _lib.SHARD_WAIT_PREV, st))
         if not chain:
             self.sync()
         return self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
@@ -165,8 +212,8 @@ class RowShardGroup:
 
         if self.world > 1:
             st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            _lib.check(self.lib.cllm_cuda_shard_wait(ctypes.c_void_p(self._sig.data_ptr()),
-                                                     ctypes.c_void_p(self._epoch.data_ptr()), self.world, st))
+            _lib.check(self.lib.cllm_cuda_shard_wait(ctypes.c_void_p(self._sig_ptr),
+                                                     ctypes.c_void_p(self._epoch_ptr), self.world, st))
 
     def matmul_nccl(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None):
         """The same result through the local GEMV and an NCCL all-gather."""
@@ -182,4 +229,16 @@ class RowShardGroup:
         return gather_rows(local, sw.out_dim, self.group)
 
     def close(self):
-        self._handles = []
+        """Unmap the peers' buffers, then (after every rank has) free this rank's."""
+        import torch
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            _lib.check(self.lib.cllm_cuda_ipc_close(ctypes.c_void_p(p)))
+        self._opened = []
+        self._allgather(b"closed")
+        self._y = []
+        _lib.check(self.lib.cllm_cuda_ipc_free(ctypes.c_void_p(self._own)))
+        self._own = None

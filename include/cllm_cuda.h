@@ -56,7 +56,12 @@ extern "C" {
 #define CLLM_TYPE_Q6_K 14
 
 /* ---- cllm_cuda_matmul_quant flags -------------------------------------- */
-#define CLLM_X_HOST 1u /* x and bias are host pointers (copied in on the stream) */
+/* Host buffers of the GEMV path (n_rows below the tensor-core prefill) that are
+ * pinned and mapped (cudaHostAlloc, cudaMallocHost, cudaHostRegister) are used
+ * in place: x is read once by the activation-quantization kernel and y is
+ * written by the GEMV's stores, with no copy operation.  Other host buffers
+ * (pageable memory, the prefill and fallback paths) are copied on the stream. */
+#define CLLM_X_HOST 1u /* x and bias are host pointers (bias is always copied in) */
 #define CLLM_Y_HOST 2u /* y is a host pointer; the call synchronizes the stream */
 #define CLLM_W_HOST 4u /* w is a host pointer inside a range given to cllm_cuda_register_weights */
 #define CLLM_HOST_IO (CLLM_X_HOST | CLLM_Y_HOST)
@@ -253,6 +258,21 @@ int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int wor
  * Double-buffer y across consecutive calls: a rank may start writing call
  * n+1's slice while a slower rank still reads call n's y. */
 int cllm_cuda_shard_barrier(uint32_t* const* signal_pads, uint32_t* epoch, int world, int rank, void* stream);
+
+/* Peer-mapped buffers for the row-sharded calls without any framework: each
+ * rank allocates its buffer here, publishes the CLLM_IPC_HANDLE_BYTES handle
+ * to the other ranks over any host transport (MPI, a TCP store, a file), and
+ * maps every peer's buffer with cllm_cuda_ipc_open (CUDA IPC: plain NVLink
+ * peer mappings, no multicast objects).  A rank uses its own pointer for its
+ * own slot (a process cannot open its own handle).  Close peer mappings
+ * before the owners free their buffers. */
+#define CLLM_IPC_HANDLE_BYTES 64
+/* bytes of zeroed device memory on the current device, and its handle */
+int cllm_cuda_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+/* map a peer's buffer into this process */
+int cllm_cuda_ipc_open(const void* handle, void** dev_ptr);
+int cllm_cuda_ipc_close(void* dev_ptr);
+int cllm_cuda_ipc_free(void* dev_ptr);
 
 /* ---- Device-resident engine step ----------------------
  * The reference's GgufLoader::load + TransformerEngine (gguf.cpp:120-275,

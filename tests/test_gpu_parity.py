@@ -173,6 +173,40 @@ def test_host_io_and_registry(cuda, lib, oracle):
                                       None) == _lib.ERR_NOT_REGISTERED
 
 
+@pytest.mark.parametrize("t,k,n,m,xoff,yoff", [(synth.Q4_K, 4096, 500, 1, 0, 0), (synth.Q4_K, 4096, 500, 3, 0, 1),
+                                                (synth.Q4_K, 4096, 300, 9, 1, 0), (synth.Q6_K, 14336, 300, 1, 0, 0),
+                                                (synth.Q8_0, 4096, 200, 2, 0, 0)])
+def test_host_io_pinned_in_place(cuda, lib, oracle, t, k, n, m, xoff, yoff):
+    """Pinned (mapped) host x and y are used in place by the GEMV path: x read
+    by the quantization kernel, y written by the GEMV -- including x at a
+    4-byte offset (not 16-byte aligned: the unfused quantize kernel reads it)
+    and M = 9 (two row chunks)."""
+    import ctypes
+
+    w = synth.make_weights(t, n, k, seed=23)
+    x = synth.make_activations(m, k, 24)
+    bias = np.linspace(-1, 1, n, dtype=np.float32)
+    wt, wp = G.dev_bytes(w)  # wt keeps the device copy alive
+    xh = torch.empty(m * k + 4, dtype=torch.float32, pin_memory=True)
+    yh = torch.full((m * n + 4,), float("nan"), dtype=torch.float32, pin_memory=True)
+    xh[xoff:xoff + m * k] = torch.from_numpy(x.reshape(-1))
+    bias_pinned = torch.from_numpy(bias).pin_memory()
+    # a repeated call with the same pointers replays a cached graph: new x contents
+    # must be seen; a pageable bias takes the direct path
+    for b, bptr, xs in ((None, None, x), (bias, bias_pinned.data_ptr(), x),
+                        (bias, bias_pinned.data_ptr(), -0.5 * x), (bias, bias.ctypes.data, x)):
+        x = xs
+        xh[xoff:xoff + m * k] = torch.from_numpy(x.reshape(-1))
+        yh.fill_(float("nan"))
+        _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xh.data_ptr() + 4 * xoff), wp, t,
+                                              None if bptr is None else ctypes.c_void_p(bptr), k, n, m,
+                                              ctypes.c_void_p(yh.data_ptr() + 4 * yoff), _lib.HOST_IO, None))
+        y = yh[yoff:yoff + m * n].numpy().reshape(m, n)
+        yo, ab = oracle.matmul(x, w, t, k, n, bias=b, with_abs=True)
+        G.assert_rows_close(y, yo, ab, REL_TOL, f"pinned host io {synth.NAMES[t]} m={m}")
+        assert np.isnan(yh[:yoff].numpy()).all() and np.isnan(yh[yoff + m * n:].numpy()).all()
+
+
 def test_empty_and_degenerate(cuda, lib, oracle):
     t = synth.Q4_K
     w = synth.make_weights(t, 8, 256, 1)

@@ -101,3 +101,65 @@ def test_gather_rows_two_gloo_ranks(oracle):
         w = synth.make_weights(t, n, k, seed=seed)
         x = synth.make_activations(m, k, seed + 1)
         assert np.array_equal(y, oracle.matmul(x, w, t, k, n))
+
+
+class _FakeIpcLib:
+    """Stands in for the C ABI's cllm_cuda_ipc_alloc / _open on a CPU-only
+    host: rank r's buffer is address 0x10000 * (r + 1), its handle 64 bytes of
+    r + 1; opening a handle returns 0x7000_0000 + that address."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened = []
+
+    def cllm_cuda_ipc_alloc(self, nbytes, ptr_ref, handle):
+        ptr_ref._obj.value = 0x10000 * (self.rank + 1)
+        for i in range(len(handle)):
+            handle[i] = self.rank + 1
+        return 0
+
+    def cllm_cuda_ipc_open(self, handle, ptr_ref):
+        owner = handle[0] - 1
+        assert all(b == owner + 1 for b in handle) and owner != self.rank
+        ptr_ref._obj.value = 0x70000000 + 0x10000 * (owner + 1)
+        self.opened.append(owner)
+        return 0
+
+
+def _ipc_worker(rank, world, port, result_q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        lib = _FakeIpcLib(rank)
+        own, ptrs, opened = sharded.open_peer_buffers(lib, 4096, rank, world, sharded._torch_allgather(None))
+        result_q.put((rank, own, ptrs, opened, lib.opened))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_buffer_exchange_two_gloo_ranks():
+    """The handle exchange of RowShardGroup (open_peer_buffers) over gloo:
+    each rank's own slot is its own allocation, every other slot the mapping
+    of that rank's published handle, and a process never opens its own."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ipc_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=240) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, own, ptrs, opened, opened_owners in got:
+        assert own == 0x10000 * (rank + 1)
+        assert ptrs[rank] == own
+        other = 1 - rank
+        assert ptrs[other] == 0x70000000 + 0x10000 * (other + 1)
+        assert opened == [ptrs[other]] and opened_owners == [other]
