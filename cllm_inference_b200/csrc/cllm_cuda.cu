@@ -90,6 +90,9 @@ struct DeviceInfo {
     // operations: bit 0 reads x in place, bit 1 writes y in place (environment
     // CLLM_HOSTIO_DIRECT, 0..3).
     int hostio_direct = 3;
+    // Q4_K rows of 16..32 super-blocks on the lane-per-super-block loop
+    // (environment CLLM_GEMV_SB=0: the lane-per-unit loop instead).
+    int gemv_sb = 1;
 };
 
 std::mutex g_mu;
@@ -134,6 +137,7 @@ int ensure_device(int* out_dev) {
         di.max_smem_optin = prop.sharedMemPerBlockOptin;
         if (const char* v = std::getenv("CLLM_GEMV_CTAS_PER_SM")) di.gemv_ctas_per_sm = std::atoi(v) == 1 ? 1 : 2;
         if (const char* v = std::getenv("CLLM_HOSTIO_DIRECT")) di.hostio_direct = std::atoi(v) & 3;
+        if (const char* v = std::getenv("CLLM_GEMV_SB")) di.gemv_sb = std::atoi(v) != 0;
         di.ready = true;
     }
     *out_dev = dev;
@@ -228,7 +232,7 @@ GemvFn select_gemv(int type, bool tma, bool fused, bool emit, int m) {
     return nullptr;
 }
 
-typedef void (*ImageFn)(const float*, int, uint8_t*, const uint32_t*, const uint32_t*, int, const PreOp);
+typedef void (*ImageFn)(const float*, int, uint8_t*, const uint32_t*, const uint32_t*, int, const PreOp, int);
 
 template <int T>
 ImageFn image_fn(int m) {
@@ -270,7 +274,7 @@ uint32_t image_bytes(int m, int K) { return (uint32_t)kImageHeader + fused_act_b
 // announcement of round *wait_epoch before reading x; nullptr: no wait.
 int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas, cudaStream_t st,
                  const uint32_t* wait_pad = nullptr, const uint32_t* wait_epoch = nullptr, int wait_world = 0,
-                 PreOp pre = PreOp{kPreNone, nullptr, 0.0f}) {
+                 PreOp pre = PreOp{kPreNone, nullptr, 0.0f}, bool sb_layout = false) {
     ImageFn fn = select_image(type, m);
     if (!fn) return fail(CLLM_ERR_INVALID_ARG, "no activation-image kernel for type %d, %d rows", type, m);
     const int groups = (m * (K / 32) + kGemvThreads / 4 - 1) / (kGemvThreads / 4);
@@ -284,7 +288,7 @@ int launch_image(int type, int m, const float* x, int K, uint8_t* img, int* ctas
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img, wait_pad, wait_epoch, wait_world, pre));
+    CLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, x, K, img, wait_pad, wait_epoch, wait_world, pre, sb_layout ? 1 : 0));
     *ctas = n;
     return CLLM_OK;
 }
@@ -296,6 +300,7 @@ constexpr uint32_t kFusedActMax = 48 * 1024;  // largest quantized activation ke
 struct GemvPlan {
     bool tma, fused;
     int rows_per_tile, wpr, num_tiles, stages, grid;
+    int sb_lanes;  // > 0: the Q4_K super-block loop (q4k_row_sb), lanes per row
     uint32_t stage_bytes;
     size_t smem;
 };
@@ -318,11 +323,31 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
     pl.stage_bytes = (uint32_t)(((int64_t)R * row_bytes + 127) & ~int64_t(127));
     const uint32_t act = (fused_act_bytes(m, K) + 127u) / 128u * 128u;
     pl.fused = want_fused && K > 0 && act <= kFusedActMax;
+    // Q4_K at M = 1 with 16..32 super-blocks per row (fused): lane =
+    // super-block, every warp takes 32 / sb_lanes whole rows of the tile; the
+    // fused quantization writes the matching activation layout.  (At M > 1 the
+    // lane-per-unit loop is faster: its per-token scale loads are free of bank
+    // conflicts.)
+    pl.sb_lanes = 0;
+    // Rows of 16 super-blocks pair up in 16-row tiles; with fewer tiles than SMs
+    // the lane-per-unit loop's 8-row tiles spread the call wider.
+    const int sb_lanes = K >= 32 * 256 ? 32 : 16;
+    const bool sb_wide = sb_lanes == 32 || (N + 2 * kGemvWarps - 1) / (2 * kGemvWarps) >= di.sms;
+    if (pl.fused && m == 1 && type == kQ4_K && act_sb_layout<kQ4_K, 1>(K) && di.gemv_sb && sb_wide) {
+        pl.sb_lanes = sb_lanes;
+        pl.rows_per_tile = kGemvWarps * (32 / pl.sb_lanes);
+        pl.wpr = 1;
+        pl.num_tiles = (N + pl.rows_per_tile - 1) / pl.rows_per_tile;
+        pl.stage_bytes = (uint32_t)(((int64_t)pl.rows_per_tile * row_bytes + 127) & ~int64_t(127));
+    }
     const size_t fixed = kGemvSmemHeader + (pl.fused ? act : 0);
     const size_t limit = di.max_smem_optin > 1024 ? di.max_smem_optin - 1024 : 0;
     pl.tma = K > 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (row_bytes & 15) == 0 &&
              fixed + 2ull * pl.stage_bytes <= limit;
-    if (!pl.tma) pl.fused = false;
+    if (!pl.tma) {
+        pl.fused = false;
+        if (pl.sb_lanes) return plan_gemv(type, w, row_bytes, K, N, m, false, di, x);
+    }
     if (pl.tma) {
         const size_t budget = std::max<size_t>(kSmemPerCta, fixed + 2ull * pl.stage_bytes);
         int S = (int)std::min<size_t>(8, (budget - fixed) / pl.stage_bytes);
@@ -335,8 +360,11 @@ GemvPlan plan_gemv(int type, const uint8_t* w, int64_t row_bytes, int K, int N, 
         // rounds: every CTA then gets the same number of tiles (within one),
         // so none idles through the last round (gate/up 14336x4096: 296 CTAs
         // with 6 or 7 tiles -> 256 CTAs with 7, 6.6 % faster).
+        // (The super-block loop's 16-row tiles are too coarse for that: it keeps
+        // every CTA slot, so that no SM runs two CTAs' worth of tiles while
+        // another runs one.)
         const int rounds = (pl.num_tiles + pl.grid - 1) / pl.grid;
-        if (rounds <= 16) pl.grid = (pl.num_tiles + rounds - 1) / rounds;
+        if (rounds <= 16 && !pl.sb_lanes) pl.grid = (pl.num_tiles + rounds - 1) / rounds;
     } else {
         pl.stages = 0;
         pl.smem = 0;
@@ -393,6 +421,7 @@ int launch_gemv(int type, bool emit, int m, const GemvPlan& pl, const GemvParams
 }
 
 void fill_plan(GemvParams& p, const GemvPlan& pl) {
+    p.sb_lanes = pl.sb_lanes;
     p.rows_per_tile = pl.rows_per_tile;
     p.wpr = pl.wpr;
     p.num_tiles = pl.num_tiles;
@@ -644,7 +673,9 @@ int run_decode(int type, const uint8_t* wd, int64_t row_bytes, const float* xd, 
                                          const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
                 return rc;
         } else if (img && pl.tma) {
-            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st, nullptr, nullptr, 0, pre)) return rc;
+            if (int rc = launch_image(type, m, p.x, in_dim, img, &p.image_ctas, st, nullptr, nullptr, 0, pre,
+                                      pl.sb_lanes != 0))
+                return rc;
             p.image = img;
             p.image_bytes = image_bytes(m, in_dim);
         } else {
@@ -1361,7 +1392,7 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     if (use_image) {
         const bool w = wait_prev && signal_pads;
         if (int rc = launch_image(type, n_rows, x, in_dim, ws, &p.image_ctas, st, w ? signal_pads[rank] : nullptr,
-                                  w ? epoch : nullptr, w ? world : 0))
+                                  w ? epoch : nullptr, w ? world : 0, PreOp{kPreNone, nullptr, 0.0f}, pl.sb_lanes != 0))
             return rc;
         p.image = ws;
         p.image_bytes = image_bytes(n_rows, in_dim);

@@ -57,6 +57,7 @@ struct GemvParams {
     int num_tiles;
     int stages;
     uint32_t stage_bytes;
+    int sb_lanes;         // > 0: Q4_K super-block loop (q4k_row_sb), lanes per row
     int64_t ldy;          // row stride of y (0: N); set per launch
     int npeers;           // > 0: row-sharded call, y goes to every ypeers[q] instead of y
     float* ypeers[kMaxPeers];
@@ -216,6 +217,21 @@ __host__ __device__ __forceinline__ uint32_t act_swizzle(uint32_t off) {
 }
 
 __host__ __device__ __forceinline__ int act_row_stride(int K) { return (K + 127) & ~127; }
+
+// Q4_K with 16..32 super-blocks per row may run q4k_row_sb (lane =
+// super-block; the plan's sb_lanes).  Its lanes read 16-byte slot c of
+// super-blocks s, s+1, ... at once, so with that plan the activation writers
+// swizzle the slots of a super-block with the super-block index instead
+// (slot ^= (slot >> 4) & 7): eight consecutive super-blocks then hit eight
+// different 16-byte bank groups.
+template <int TYPE, int M>
+__host__ __device__ __forceinline__ bool act_sb_layout(int K) {
+    return TYPE == kQ4_K && K >= 4096 && K <= 8192;
+}
+__host__ __device__ __forceinline__ uint32_t act_swizzle_sb(uint32_t off) {
+    const uint32_t slot = off >> 4;
+    return ((slot ^ ((slot >> 4) & 7u)) << 4) | (off & 15u);
+}
 
 __device__ __forceinline__ uint2 lds64(uint32_t a) {
     uint2 v;
@@ -571,6 +587,91 @@ __device__ __forceinline__ void q4k_row_fused(uint32_t wrow, const ActSmem<kQ4_K
 }
 
 
+// Q4_K row with lane = super-block (quant.cpp:549-590), M <= 8 activation
+// rows: the `lanes` lanes of a weight row take its super-blocks li,
+// li + lanes, ...; a super-block's scales are decoded once for its 256 values,
+// and each activation row arrives as 16-byte loads (layout act_swizzle_sb).
+// Per 32-value block the same integer partial and the same two FMA statements
+// as q4k_row_fused.  EMIT: also store each block's partial at
+// prow[t * pstride + block].
+template <int M, bool EMIT>
+__device__ __forceinline__ void q4k_row_sb(uint32_t wrow, const ActSmem<kQ4_K>& act, int nsb, int li, int lanes,
+                                           float (&acc)[M], int32_t* prow, int64_t pstride) {
+#pragma unroll
+    for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+    for (int s = li; s < nsb; s += lanes) {
+        const uint32_t wb = wrow + 144u * (uint32_t)s;
+        const uint4 h = lds128(wb);
+        const float d = h2f(h.x), dmin = h2f(h.x >> 16);
+        const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+        const uint32_t key = (uint32_t)s & 7u;
+        uint32_t dxw[8], bsw[8];  // M = 1: the eight blocks' (dx, bsum) in four loads
+        if constexpr (M == 1) {
+            const uint32_t da = act.dx + 32u * (uint32_t)s, ba = act.bs + 32u * (uint32_t)s;
+            const uint4 d0 = lds128(da), d1 = lds128(da + 16u), q0 = lds128(ba), q1 = lds128(ba + 16u);
+            dxw[0] = d0.x; dxw[1] = d0.y; dxw[2] = d0.z; dxw[3] = d0.w;
+            dxw[4] = d1.x; dxw[5] = d1.y; dxw[6] = d1.z; dxw[7] = d1.w;
+            bsw[0] = q0.x; bsw[1] = q0.y; bsw[2] = q0.z; bsw[3] = q0.w;
+            bsw[4] = q1.x; bsw[5] = q1.y; bsw[6] = q1.z; bsw[7] = q1.w;
+        }
+#pragma unroll
+        for (int pq = 0; pq < 4; ++pq) {
+            // quant bytes of sub-blocks 2pq (low nibbles) and 2pq+1 (high nibbles)
+            const uint4 wa = lds128(wb + 16u + 32u * pq), wc = lds128(wb + 32u + 32u * pq);
+            const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
+            int lo[8];
+            uint32_t hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                lo[i] = (int)(w[i] & 0x0F0F0F0Fu);
+                hi[i] = w[i] & 0xF0F0F0F0u;  // 16 x high nibble, unsigned
+            }
+            const uint32_t scw = pq < 2 ? sc_lo : sc_hi, mw = pq < 2 ? m_lo : m_hi;
+            const uint32_t sel0 = (uint32_t)(pq & 1) * 2u, sel1 = sel0 + 1u;
+            const float d1 = d * byte_as_float(scw, sel0), d2 = d * byte_as_float(scw, sel1);
+            const float m1 = dmin * byte_as_float(mw, sel0), m2 = dmin * byte_as_float(mw, sel1);
+            const int b0 = 8 * s + 2 * pq;  // block of sub-block 2pq
+#pragma unroll
+            for (int t = 0; t < M; ++t) {
+                const uint32_t xrow = act.qx + (uint32_t)(t * act.kp) + 256u * (uint32_t)s;
+                const uint4 x0 = lds128(xrow + 16u * ((4u * pq) ^ key));
+                const uint4 x1 = lds128(xrow + 16u * ((4u * pq + 1u) ^ key));
+                const uint4 x2 = lds128(xrow + 16u * ((4u * pq + 2u) ^ key));
+                const uint4 x3 = lds128(xrow + 16u * ((4u * pq + 3u) ^ key));
+                int P0 = dp4a(lo[0], (int)x0.x, 0);
+                P0 = dp4a(lo[1], (int)x0.y, P0); P0 = dp4a(lo[2], (int)x0.z, P0); P0 = dp4a(lo[3], (int)x0.w, P0);
+                P0 = dp4a(lo[4], (int)x1.x, P0); P0 = dp4a(lo[5], (int)x1.y, P0);
+                P0 = dp4a(lo[6], (int)x1.z, P0); P0 = dp4a(lo[7], (int)x1.w, P0);
+                int H1 = dp4a_us(hi[0], (int)x2.x, 0);
+                H1 = dp4a_us(hi[1], (int)x2.y, H1); H1 = dp4a_us(hi[2], (int)x2.z, H1); H1 = dp4a_us(hi[3], (int)x2.w, H1);
+                H1 = dp4a_us(hi[4], (int)x3.x, H1); H1 = dp4a_us(hi[5], (int)x3.y, H1);
+                H1 = dp4a_us(hi[6], (int)x3.z, H1); H1 = dp4a_us(hi[7], (int)x3.w, H1);
+                const int P1 = H1 >> 4;  // exact: every term is a multiple of 16
+                if constexpr (EMIT) {
+                    prow[t * pstride + b0] = P0;
+                    prow[t * pstride + b0 + 1] = P1;
+                }
+                uint2 dd, ss;
+                if constexpr (M == 1) {
+                    dd = make_uint2(dxw[2 * pq], dxw[2 * pq + 1]);
+                    ss = make_uint2(bsw[2 * pq], bsw[2 * pq + 1]);
+                } else {
+                    const uint32_t sa = 4u * (uint32_t)(t * act.nb + b0);
+                    dd = lds64(act.dx + sa);
+                    ss = lds64(act.bs + sa);
+                }
+                const float dx0 = __uint_as_float(dd.x), dx1 = __uint_as_float(dd.y);
+                acc[t] = fmaf(d1 * dx0, i2f_exact(P0), acc[t]);
+                acc[t] = fmaf(-(m1 * dx0), i2f_exact((int)ss.x), acc[t]);
+                acc[t] = fmaf(d2 * dx1, i2f_exact(P1), acc[t]);
+                acc[t] = fmaf(-(m2 * dx1), i2f_exact((int)ss.y), acc[t]);
+            }
+        }
+    }
+}
+
 // 8 words of a 32-byte field at shared address a, which is 4-byte aligned
 // (odd == false) or 2 bytes past a 4-byte boundary (odd == true).
 __device__ __forceinline__ void lds_field8(uint32_t a, bool odd, uint32_t (&w)[8]) {
@@ -878,7 +979,8 @@ __device__ __forceinline__ void pre_apply(const PreOp& pre, const float* s_rms, 
 template <int M, int TYPE, bool GLOBAL>
 __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x, int K, uint8_t* qs, float* dx,
                                                     int* bs, int* hs, int gfirst, int gcount,
-                                                    const PreOp& pre, const float* s_rms) {
+                                                    const PreOp& pre, const float* s_rms, bool sb_layout) {
+    // sb_layout: the slot swizzle of the lane-per-super-block loop (act_swizzle_sb)
     // gfirst: this CTA's first group of blocks; gcount: groups per pass of all
     // CTAs taking part (one CTA: 0 and 64).  Returns this thread's row mask.
     const int kp = act_row_stride(K);
@@ -941,7 +1043,8 @@ __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x,
             if (blk < total) {
                 const int t = blk / nb, b = blk - t * nb;
                 const int pb = act_perm<TYPE>(b, nb);
-                const uint32_t off = (uint32_t)(t * kp) + act_swizzle(32u * pb + 8u * sub);
+                const uint32_t lo = 32u * pb + 8u * sub;
+                const uint32_t off = (uint32_t)(t * kp) + (sb_layout ? act_swizzle_sb(lo) : act_swizzle(lo));
                 if constexpr (GLOBAL) {
                     *reinterpret_cast<uint2*>(qs + off) = make_uint2(w0, w1);
                 } else {
@@ -967,9 +1070,10 @@ __device__ __forceinline__ uint32_t quantize_blocks(const float* __restrict__ x,
 template <int M, int TYPE>
 __device__ __forceinline__ uint32_t quantize_to_smem(const float* __restrict__ x, int K,
                                                      uint8_t* qs, float* dx, int* bs, int* hs,
-                                                     uint32_t* s_quirk, const PreOp& pre, float* s_pre) {
+                                                     uint32_t* s_quirk, const PreOp& pre, float* s_pre, bool sb_layout) {
     if (pre.op == kPreRmsNorm) pre_rms<M>(x, K, pre.eps, s_pre, s_pre + 64);
-    const uint32_t mask = quantize_blocks<M, TYPE, false>(x, K, qs, dx, bs, hs, 0, kGemvThreads / 4, pre, s_pre + 64);
+    const uint32_t mask =
+        quantize_blocks<M, TYPE, false>(x, K, qs, dx, bs, hs, 0, kGemvThreads / 4, pre, s_pre + 64, sb_layout);
     // OR over the compute warps (*s_quirk is zero on entry), then a barrier
     // over those warps only: the producer warp does not take part.
     const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
@@ -988,7 +1092,7 @@ template <int M, int TYPE>
 __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __restrict__ x, int K,
                                                                  uint8_t* __restrict__ image, const uint32_t* wait_pad,
                                                                  const uint32_t* wait_epoch, int wait_world,
-                                                                 const PreOp pre) {
+                                                                 const PreOp pre, int sb_layout) {
     __shared__ uint32_t s_mask;
     __shared__ float s_pre[64 + 8];
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1018,7 +1122,8 @@ __global__ void __launch_bounds__(kGemvThreads) act_image_kernel(const float* __
     int* bs = reinterpret_cast<int*>(qs + qbytes + 4u * (uint32_t)(M * nb));
     int* hs = reinterpret_cast<int*>(qs + qbytes + 8u * (uint32_t)(M * nb));
     const uint32_t mask = quantize_blocks<M, TYPE, true>(x, K, qs, dx, bs, hs, (int)blockIdx.x * (kGemvThreads / 4),
-                                                         (int)gridDim.x * (kGemvThreads / 4), pre, s_pre + 64);
+                                                         (int)gridDim.x * (kGemvThreads / 4), pre, s_pre + 64,
+                                                         sb_layout != 0);
     const uint32_t wm = __reduce_or_sync(0xFFFFFFFFu, mask);
     if ((threadIdx.x & 31) == 0 && wm) atomicOr(&s_mask, wm);
     __syncthreads();
@@ -1131,7 +1236,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
             for (int c = 0; c < p.image_ctas; ++c) qm |= masks[c];
         } else {
             qm = quantize_to_smem<M, TYPE>(p.x, p.K, qs, dxs, bss, hss, s_quirk, p.pre,
-                                           reinterpret_cast<float*>(smem + kHdrPre));
+                                           reinterpret_cast<float*>(smem + kHdrPre), p.sb_lanes != 0);
         }
         quirk = (TYPE == kQ8_0 || TYPE == kQ6_K) ? qm : 0u;
         as = ActSmem<TYPE>{smem_addr(qs), smem_addr(dxs), smem_addr(bss), smem_addr(hss), act_row_stride(p.K), nb};
@@ -1146,6 +1251,32 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         if (!mbar_wait_or_abort(full0 + 8 * stg, (uint32_t)(it / S) & 1u, s_abort)) break;
         const int row0 = tile * p.rows_per_tile;
         const int rows = min(p.rows_per_tile, p.N - row0);
+        if constexpr (FUSED && TYPE == kQ4_K) {
+            if (p.sb_lanes) {  // lane = super-block: this warp takes 32 / sb_lanes rows of the tile
+                const int lanes = p.sb_lanes, li = lane & (lanes - 1);
+                const int rr = warp * (32 / lanes) + lane / lanes;
+                float acc[M];
+#pragma unroll
+                for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+                if (rr < rows) {
+                    int32_t* prow = EMIT ? p.partials + (int64_t)(row0 + rr) * nb : nullptr;
+                    q4k_row_sb<M, EMIT>(ring + stg * p.stage_bytes + (uint32_t)(rr * p.row_bytes), as, p.K >> 8, li,
+                                        lanes, acc, prow, (int64_t)p.N * nb);
+                }
+#pragma unroll
+                for (int t = 0; t < M; ++t)
+                    for (int o = lanes >> 1; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xFFFFFFFFu, acc[t], o);
+                if (!EMIT && li == 0 && rr < rows) {
+                    const int j = row0 + rr;
+                    const float b = p.bias ? p.bias[j] : 0.0f;
+#pragma unroll
+                    for (int t = 0; t < M; ++t) gemv_put(p, t, j, acc[t] + b);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8 * stg);
+                continue;
+            }
+        }
         if (r < rows) {
             float acc[M];
             SmemSrc src{ring + stg * p.stage_bytes + (uint32_t)(r * p.row_bytes)};

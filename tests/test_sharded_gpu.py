@@ -236,6 +236,7 @@ def _two_gpu_worker(rank, world, port, q):
             ok &= bool(np.all(np.abs(yn.astype(np.float64) - y_ref) <= 1e-5 * a_ref + 1e-30))
         torch.cuda.synchronize()
         ok &= lib.cllm_cuda_check_device_status() == 0
+        grp.close()
         dist.barrier()
     finally:
         q.put((rank, ok))
