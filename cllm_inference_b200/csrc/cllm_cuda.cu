@@ -487,12 +487,24 @@ bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_r
 // Tokens per row of the Q6_K block-major dx array (16-byte rows for its tensor map).
 inline int64_t q6_dx_pitch(int M) { return ((int64_t)M + 3) & ~int64_t(3); }
 
+// Split-K factor of the Q6_K prefill: with fewer 128x128 tiles than SMs, enough
+// K splits to give every SM a CTA (at least four super-blocks each, at most 8).
+int q6_splits(int M, int N, int K, int sms) {
+    const int tiles = ((M + kTcBM - 1) / kTcBM) * ((N + kTcBN - 1) / kTcBN);
+    if (tiles >= sms) return 1;
+    return std::max(1, std::min({sms / tiles, (K >> 8) / 4, 8}));
+}
+
 // Workspace bytes of the prefill activations for M rows of K: fp16 q_x, then
-// (dx, dx*bsum) [M][nb] for Q4_K, or dx [nb][pitch] and the -128 flags [M][nb] for Q6_K.
-size_t prefill_bytes(int type, int M, int K) {
+// (dx, dx*bsum) [M][nb] for Q4_K, or dx [nb][pitch], the -128 flags [M][nb]
+// and the split-K partial sums [splits][M][N] for Q6_K.
+size_t prefill_bytes(int type, int M, int N, int K, int sms) {
     const size_t nb = (size_t)K / 32;
-    if (type == kQ6_K)
-        return align256((size_t)M * K * 2) + align256(nb * (size_t)q6_dx_pitch(M) * 4) + align256((size_t)M * nb);
+    if (type == kQ6_K) {
+        const int sp = q6_splits(M, N, K, sms);
+        return align256((size_t)M * K * 2) + align256(nb * (size_t)q6_dx_pitch(M) * 4) + align256((size_t)M * nb) +
+               (sp > 1 ? align256((size_t)sp * M * N * 4) : 0);
+    }
     return align256((size_t)M * K * 2) + align256((size_t)M * nb * 8);
 }
 
@@ -504,6 +516,8 @@ int launch_prefill_q6k(const float* x, const uint8_t* w, int64_t row_bytes, cons
     __half* a16 = reinterpret_cast<__half*>(ws);
     float* dxT = reinterpret_cast<float*>(ws + align256((size_t)M * K * 2));
     uint8_t* flags = ws + align256((size_t)M * K * 2) + align256((size_t)(nb * mp * 4));
+    const int splits = q6_splits(M, N, K, di.sms);
+    float* ypart = splits > 1 ? reinterpret_cast<float*>(flags + align256((size_t)(M * nb))) : nullptr;
     const int64_t blocks = (int64_t)M * nb;
     const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
     prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, nullptr, dxT, mp, flags);
@@ -519,17 +533,18 @@ int launch_prefill_q6k(const float* x, const uint8_t* w, int64_t row_bytes, cons
                              kTcBN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
     if (int rc = opt_in_smem(reinterpret_cast<const void*>(prefill_q6k_kernel), dev)) return rc;
-    const Q6Params qp{M, N, K, bias, y};
-    const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN);
+    const Q6Params qp{M, N, K, bias, y, splits, ypart};
+    const dim3 tgrid((M + kTcBM - 1) / kTcBM, (N + kTcBN - 1) / kTcBN, splits);
     prefill_q6k_kernel<<<tgrid, kTcThreads, kQ6SmemBytes, st>>>(map_x, map_w, map_dx, qp);
     CLLM_CUDA_TRY(cudaGetLastError());
-    prefill_q6k_fixup_kernel<<<(unsigned)M, 128, 0, st>>>(w, row_bytes, a16, dxT, mp, flags, K, N, y);
+    prefill_q6k_finish_kernel<<<(unsigned)M, 128, 0, st>>>(w, row_bytes, a16, dxT, mp, flags, K, M, N, bias, splits,
+                                                            ypart, y);
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }
 
 // y[M][N] = batch matmul through the tcgen05 kernel of the weight type; x, w,
-// bias, y on the device, ws = prefill_bytes(type, M, K) of workspace.
+// bias, y on the device, ws = prefill_bytes(type, M, N, K, sms) of workspace.
 int launch_prefill(int type, const float* x, const uint8_t* w, int64_t row_bytes, const float* bias, int K, int N,
                    int M, float* y, uint8_t* ws, int dev, cudaStream_t st) {
     if (type == kQ6_K) return launch_prefill_q6k(x, w, row_bytes, bias, K, N, M, y, ws, dev, st);
@@ -755,7 +770,7 @@ int matmul_quant_impl(const float* x, const void* w, int type, const float* bias
         total = align256(total + (size_t)n_rows * out_dim * 4);
     }
     const size_t off_pre = total;
-    if (use_tc) total += prefill_bytes(type, n_rows, in_dim);
+    if (use_tc) total += prefill_bytes(type, n_rows, out_dim, in_dim, di.sms);
     const size_t off_img = total;
     // a mapped x goes through the activation image so that it crosses the host link once
     const bool want_image = gemv_path && (in_dim >= kImageMinK || x_map);
@@ -1236,7 +1251,8 @@ int cllm_cuda_matmul_plan(const void* w, int type, int in_dim, int out_dim, int 
         vals[3] = kTcBN;
         vals[4] = 0;
         vals[5] = kTcStA;
-        vals[6] = ((n_rows + kTcBM - 1) / kTcBM) * ((out_dim + kTcBN - 1) / kTcBN);
+        vals[6] = ((n_rows + kTcBM - 1) / kTcBM) * ((out_dim + kTcBN - 1) / kTcBN) *
+                  (type == kQ6_K ? q6_splits(n_rows, out_dim, in_dim, g_dev[dev].sms) : 1);
         vals[7] = (int)(type == kQ6_K ? kQ6SmemBytes : kTcSmemBytes);
     }
     for (int i = 0; i < n_info && i < 8; ++i) info[i] = vals[i];

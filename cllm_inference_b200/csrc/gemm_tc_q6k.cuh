@@ -23,8 +23,11 @@
 // The AVX2 dot negates the activation byte where the weight is negative
 // (quant.cpp:676-679); -(-128) wraps, so an activation of -128 (produced only
 // by a NaN input, quant.cpp:444-447) against a weight w < 0 contributes
-// 128*w.  The tensor core computes -128*w; prefill_q6k_fixup_kernel adds the
+// 128*w.  The tensor core computes -128*w; prefill_q6k_finish_kernel adds the
 // difference 256*w for the (token, block) pairs the preparation flagged.
+//
+// Few tiles (small M): split-K over blockIdx.z, the partial sums summed by
+// prefill_q6k_finish_kernel in a fixed order.
 //
 // Tile: 128 weight rows x 128 tokens, K in chunks of 64.  Warp roles (14):
 //   0      producer: TMA of the raw super-blocks (224-byte boxes from the
@@ -69,6 +72,11 @@ struct Q6Params {
     int M, N, K;
     const float* bias;  // [N] or nullptr
     float* y;           // [M][N]
+    // split-K (few tiles): CTA z of `splits` takes super-blocks
+    // [z*nsb/splits, (z+1)*nsb/splits) and writes its partial sums to
+    // ypart[z][M][N] (no bias); prefill_q6k_finish_kernel adds them up
+    int splits;
+    float* ypart;
 };
 
 // tcgen05.ld of 8 consecutive columns, and its wait tied to the registers.
@@ -114,8 +122,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t sb = smem_addr(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tok0 = blockIdx.x * kTcBM, row0 = blockIdx.y * kTcBN;
-    const int nsb = p.K >> 8;        // super-blocks
-    const int nchunk = p.K / kTcBK;  // 64-value chunks
+    // this CTA's super-blocks [s0, s0 + nsb); loop counters below are local to it
+    const int nsb_all = p.K >> 8;
+    const int s0 = (int)((int64_t)blockIdx.z * nsb_all / p.splits);
+    const int nsb = (int)((int64_t)(blockIdx.z + 1) * nsb_all / p.splits) - s0;
+    const int nchunk = 4 * nsb;  // 64-value chunks
     auto bar = [&](int i) { return sb + kQ6OffBar + 8u * (uint32_t)i; };
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kQ6OffAbort);
     volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(smem + kQ6OffTmem);
@@ -156,15 +167,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     !mbar_wait_or_abort(bar(kQ6RawEmpty + rs), (uint32_t)((s / kQ6StRaw) - 1) & 1u, s_abort))
                     break;
                 mbar_arrive_expect_tx(bar(kQ6RawFull + rs), kQ6RawBytes);
-                // the box starts at the 16-byte boundary at or below byte 210*s of each row
-                tma_load_2d(sb + kQ6OffRaw + rs * kQ6RawBytes, &map_w, (int)((210u * (uint32_t)s) & ~15u), row0,
+                // the box starts at the 16-byte boundary at or below byte 210*sg of each row
+                const int sg = s0 + s;
+                tma_load_2d(sb + kQ6OffRaw + rs * kQ6RawBytes, &map_w, (int)((210u * (uint32_t)sg) & ~15u), row0,
                             bar(kQ6RawFull + rs));
                 ++issued_raw;
                 const int xs = s & 1;
                 if (s >= 2 && !mbar_wait_or_abort(bar(kQ6DxEmpty + xs), (uint32_t)((s >> 1) - 1) & 1u, s_abort))
                     break;
                 mbar_arrive_expect_tx(bar(kQ6DxFull + xs), kQ6DxBytes);
-                tma_load_2d(sb + kQ6OffDx + xs * kQ6DxBytes, &map_dx, tok0, 8 * s, bar(kQ6DxFull + xs));
+                tma_load_2d(sb + kQ6OffDx + xs * kQ6DxBytes, &map_dx, tok0, 8 * sg, bar(kQ6DxFull + xs));
                 ++issued_dx;
                 for (int q = 0; q < 4; ++q) {
                     const int c = 4 * s + q, as = c % kQ6StX;
@@ -172,7 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         !mbar_wait_or_abort(bar(kQ6XEmpty + as), (uint32_t)((c / kQ6StX) - 1) & 1u, s_abort))
                         break;
                     mbar_arrive_expect_tx(bar(kQ6XFull + as), kTcTileBytes);
-                    tma_load_2d(sb + kQ6OffX + as * kTcTileBytes, &map_x, kTcBK * c, tok0, bar(kQ6XFull + as));
+                    tma_load_2d(sb + kQ6OffX + as * kTcTileBytes, &map_x, kTcBK * (4 * sg + q), tok0,
+                                bar(kQ6XFull + as));
                     ++issued_x;
                 }
             }
@@ -224,7 +237,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int rs = s % kQ6StRaw;
             if (!mbar_wait_or_abort(bar(kQ6RawFull + rs), (uint32_t)(s / kQ6StRaw) & 1u, s_abort)) break;
             // super-block layout (quant.cpp:630-687): ql[128], qh[64], int8 scales[16], fp16 d
-            const uint32_t rb = sb + kQ6OffRaw + rs * kQ6RawBytes + kQ6RawRow * (uint32_t)i + ((210u * (uint32_t)s) & 15u);
+            const uint32_t rb =
+                sb + kQ6OffRaw + rs * kQ6RawBytes + kQ6RawRow * (uint32_t)i + ((210u * (uint32_t)(s0 + s)) & 15u);
             const float d = h2f(lds16(rb + 208u));
             uint32_t scw[4];
             lds_words_a2<4>(rb + 192u, scw);
@@ -284,9 +298,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int quad = warp & 3, half = (warp - 6) >> 2;
         const int rl = 32 * quad + lane;  // weight row within the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
-        float acc[64];
+        float2 acc[32];  // tokens (2i, 2i+1) of this thread's 64
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+        for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
         for (int s = 0; s < nsb; ++s) {
             const int ss = s & 1;
             if (!warp_wait(bar(kQ6DxFull + ss), (uint32_t)(s >> 1) & 1u, s_abort)) break;
@@ -304,9 +318,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 const float sa = lds32f(sca + 4u * (uint32_t)(kTcBN * (2 * k))),
                             sbh = lds32f(sca + 4u * (uint32_t)(kTcBN * (2 * k + 1)));
+                const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sbh, sbh);
                 const uint32_t dcol = tmem + lane_base + (uint32_t)(db * 2 * kTcBM + 64 * half);
                 const uint32_t dxk = dxa + 4u * (uint32_t)(kTcBM * k);
-                // groups of 8 tokens; the TMEM loads of group g+1 overlap the FMAs of group g
+                // groups of 8 tokens; the TMEM loads of group g+1 overlap the math of group g,
+                // which runs on packed f32x2 operations (two tokens per instruction)
                 uint32_t lo[2][8], hi[2][8];
                 tmem_ld8_issue(dcol, lo[0]);
                 tmem_ld8_issue(dcol + kTcBM, hi[0]);
@@ -319,12 +335,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         tmem_ld8_issue(dcol + kTcBM + 8u * (g + 1), hi[cur ^ 1]);
                     }
                     const float4 x0 = lds128f(dxk + 32u * g), x1 = lds128f(dxk + 32u * g + 16u);
-                    const float dxv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const float2 dxv[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w),
+                                           make_float2(x1.x, x1.y), make_float2(x1.z, x1.w)};
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float u = sa * __uint_as_float(lo[cur][j]);
-                        u = fmaf(sbh, __uint_as_float(hi[cur][j]), u);
-                        acc[8 * g + j] = fmaf(dxv[j], u, acc[8 * g + j]);
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 l = make_float2(__uint_as_float(lo[cur][2 * j]), __uint_as_float(lo[cur][2 * j + 1]));
+                        const float2 h = make_float2(__uint_as_float(hi[cur][2 * j]), __uint_as_float(hi[cur][2 * j + 1]));
+                        float2 u = __fmul2_rn(sa2, l);
+                        u = __ffma2_rn(sb2, h, u);
+                        acc[4 * g + j] = __ffma2_rn(dxv[j], u, acc[4 * g + j]);
                     }
                     if (g < 7) tmem_ld_wait2(lo[cur ^ 1], hi[cur ^ 1]);
                 }
@@ -339,15 +358,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_arrive(bar(kQ6DxEmpty + ss));
             }
         }
-        // y[t][row0 + rl] (+ bias): the 32 lanes of a warp write 128 contiguous bytes per token
+        // y[t][row0 + rl] (+ bias), or this split's partial sums: the 32 lanes of a
+        // warp write 128 contiguous bytes per token
         const int aborted = __shfl_sync(0xFFFFFFFFu, *s_abort, 0);
         const int j = row0 + rl;
         if (!aborted && j < p.N) {
-            const float bj = p.bias ? p.bias[j] : 0.0f;
+            float* out = p.splits > 1 ? p.ypart + (int64_t)blockIdx.z * p.M * p.N : p.y;
+            const float bj = (p.splits == 1 && p.bias) ? p.bias[j] : 0.0f;
 #pragma unroll
             for (int tt = 0; tt < 64; ++tt) {
                 const int t = tok0 + 64 * half + tt;
-                if (t < p.M) p.y[(int64_t)t * p.N + j] = acc[tt] + bj;
+                const float v = (tt & 1) ? acc[tt >> 1].y : acc[tt >> 1].x;
+                if (t < p.M) out[(int64_t)t * p.N + j] = v + bj;
             }
         }
     }
@@ -360,41 +382,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// The AVX2 sign-trick difference for the (token, block) pairs whose q_x holds
-// -128: y[t][j] += sum_b d * dx_b * (sa * dP_lo + sb * dP_hi), dP = 256 * the
-// sum of the negative weights q6 - 32 where q_x == -128.  One CTA per token;
-// a token without a flagged block returns at once.
-__global__ void __launch_bounds__(128) prefill_q6k_fixup_kernel(const uint8_t* __restrict__ w, int64_t row_bytes,
-                                                                const __half* __restrict__ a16,
-                                                                const float* __restrict__ dxT, int64_t mp,
-                                                                const uint8_t* __restrict__ flags, int K, int N,
-                                                                float* __restrict__ y) {
+// Per token t: the sum of the split-K partials plus the bias (splits > 1),
+// and the AVX2 sign-trick difference for the (token, block) pairs whose q_x
+// holds -128: y[t][j] += sum_b d * dx_b * (sa * dP_lo + sb * dP_hi), dP = 256 *
+// the sum of the negative weights q6 - 32 where q_x == -128.  One CTA per
+// token; with one split, a token without a flagged block returns at once.
+__global__ void __launch_bounds__(128) prefill_q6k_finish_kernel(const uint8_t* __restrict__ w, int64_t row_bytes,
+                                                                 const __half* __restrict__ a16,
+                                                                 const float* __restrict__ dxT, int64_t mp,
+                                                                 const uint8_t* __restrict__ flags, int K, int M,
+                                                                 int N, const float* __restrict__ bias, int splits,
+                                                                 const float* __restrict__ ypart,
+                                                                 float* __restrict__ y) {
     const int t = blockIdx.x;
     const int nb = K >> 5;
     int any = 0;
     for (int b = threadIdx.x; b < nb; b += blockDim.x) any |= flags[(int64_t)t * nb + b];
-    if (!__syncthreads_or(any)) return;
+    any = __syncthreads_or(any);
+    if (!any && splits == 1) return;
     const __half* xq = a16 + (int64_t)t * K;
     for (int j = threadIdx.x; j < N; j += blockDim.x) {
-        const uint8_t* row = w + (int64_t)j * row_bytes;
-        float corr = 0.0f;
-        for (int b = 0; b < nb; ++b) {
-            if (!flags[(int64_t)t * nb + b]) continue;
-            const uint8_t* sbp = row + 210 * (b >> 3);
-            const int bl = b & 7, g = bl >> 2, sub = bl & 3;
-            int dp[2] = {0, 0};
-            for (int l = 0; l < 32; ++l) {
-                if (__half2float(xq[32 * b + l]) != -128.0f) continue;
-                const uint8_t raw = sbp[64 * g + 32 * (sub & 1) + l];
-                const int lo4 = sub >= 2 ? (raw >> 4) : (raw & 0xF);
-                const int q6 = (lo4 | (((sbp[128 + 32 * g + l] >> (2 * sub)) & 3) << 4)) - 32;
-                if (q6 < 0) dp[l >> 4] += 256 * q6;
-            }
-            const float d = __half2float(__ushort_as_half((unsigned short)(sbp[208] | (sbp[209] << 8))));
-            const float sa = (float)(int8_t)sbp[192 + 2 * bl], sbh = (float)(int8_t)sbp[193 + 2 * bl];
-            corr = fmaf(d * dxT[(int64_t)b * mp + t], sa * (float)dp[0] + sbh * (float)dp[1], corr);
+        float v;
+        if (splits > 1) {
+            v = 0.0f;
+            for (int z = 0; z < splits; ++z) v += ypart[((int64_t)z * M + t) * N + j];
+            if (bias) v += bias[j];
+        } else {
+            v = y[(int64_t)t * N + j];
         }
-        y[(int64_t)t * N + j] += corr;
+        if (any) {
+            const uint8_t* row = w + (int64_t)j * row_bytes;
+            float corr = 0.0f;
+            for (int b = 0; b < nb; ++b) {
+                if (!flags[(int64_t)t * nb + b]) continue;
+                const uint8_t* sbp = row + 210 * (b >> 3);
+                const int bl = b & 7, g = bl >> 2, sub = bl & 3;
+                int dp[2] = {0, 0};
+                for (int l = 0; l < 32; ++l) {
+                    if (__half2float(xq[32 * b + l]) != -128.0f) continue;
+                    const uint8_t raw = sbp[64 * g + 32 * (sub & 1) + l];
+                    const int lo4 = sub >= 2 ? (raw >> 4) : (raw & 0xF);
+                    const int q6 = (lo4 | (((sbp[128 + 32 * g + l] >> (2 * sub)) & 3) << 4)) - 32;
+                    if (q6 < 0) dp[l >> 4] += 256 * q6;
+                }
+                const float d = __half2float(__ushort_as_half((unsigned short)(sbp[208] | (sbp[209] << 8))));
+                const float sa = (float)(int8_t)sbp[192 + 2 * bl], sbh = (float)(int8_t)sbp[193 + 2 * bl];
+                corr = fmaf(d * dxT[(int64_t)b * mp + t], sa * (float)dp[0] + sbh * (float)dp[1], corr);
+            }
+            v += corr;
+        }
+        y[(int64_t)t * N + j] = v;
     }
 }
 

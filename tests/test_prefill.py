@@ -126,15 +126,17 @@ def test_prefill_q6k_ineligible_rows_take_gemv(cuda, lib):
     assert plan(lib, wp, t, k, n, m)[1] != 2
 
 
-def test_prefill_q6k_config3_down_shape(cuda, lib, oracle):
+@pytest.mark.parametrize("m", [64, 512])
+def test_prefill_q6k_config3_down_shape(cuda, lib, oracle, m):
     """The config-3 FFN down projection as Q6_K (4096 rows x 14336 in) at
-    M = 512 on the tcgen05 GEMM: three rows per 128-row tile, every token."""
-    t, k, n, m = synth.Q6_K, 14336, 4096, 512
+    M = 64 (32 tiles: split-K over four CTAs per tile) and M = 512 on the
+    tcgen05 GEMM: three rows per 128-row tile, every token."""
+    t, k, n = synth.Q6_K, 14336, 4096
     w = synth.make_weights(t, n, k, seed=4242, q6_scale_max=128)
-    x = synth.make_activations(m, k, seed=77)
+    x = synth.make_activations(m, k, seed=77 + m)
     _, wp = G.dev_bytes(w)
     assert plan(lib, wp, t, k, n, m)[1] == 2, "expected the tcgen05 path"
     y = G.matmul(lib, x, w, t, k, n)
     rows = _tile_samples(n, 128, np.random.default_rng(9))
     yo, ab = oracle.matmul(x, G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows), with_abs=True)
-    G.assert_rows_close(y[:, rows], yo, ab, REL_TOL, "config 3 down as Q6_K, M=512")
+    G.assert_rows_close(y[:, rows], yo, ab, REL_TOL, f"config 3 down as Q6_K, M={m}")
