@@ -571,13 +571,20 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
     step_bytes = sum(synth.row_bytes(w[c].type, w[c].in_dim) * w[c].out_dim + 4 * (w[c].in_dim + w[c].out_dim)
                      for c in calls)
 
+    # a call waits for every rank's previous call only where the decode step has
+    # that dependency (k and v read the same normed x as q, up the same as
+    # gate), and announces its round only where the next call waits on it
+    independent = ("k", "v", "up")
+
     def run(cs, nccl=False):
-        for c in cs:
+        for i, c in enumerate(cs):
             sw = w[c]
             if nccl:
                 grp.matmul_nccl(xs[sw.in_dim], sw, 1)
             else:
-                grp.matmul_unread(xs[sw.in_dim], sw, 1, chain=True)
+                last = i + 1 == len(cs)
+                grp.matmul_unread(xs[sw.in_dim], sw, 1, chain=True, wait=c[1] not in independent,
+                                  signal=last or cs[i + 1][1] not in independent)
         if not nccl:
             grp.sync()
 
@@ -619,7 +626,10 @@ def measure_70b(torch, dist, dev, world, rank, steps, warmup):
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "tok_s": round(1e3 / ms, 2), "bytes_per_step": step_bytes, "calls_per_step": len(calls),
             "gpus": world, "gather": "GEMV stores into every rank's y (NVLink peer mappings); its last warp "
-                                     "signals every rank; the next call waits for all signals",
+                                     "a one-warp kernel after it signals every rank; a call whose input "
+                                     "depends on the previous call (q, o, gate, down, lm_head) first waits "
+                                     "for all signals; k, v and up, which read the same x as q / gate, do "
+                                     "not, and q, k and gate do not signal",
             "first_8_layers_ms": {"fused_peer_stores": round(ms8, 4), "nccl_all_gather": round(ms8n, 4)}}
 
 

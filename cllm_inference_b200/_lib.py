@@ -27,6 +27,7 @@ ERR_TOO_LARGE = -8
 
 X_HOST, Y_HOST, W_HOST = 1, 2, 4
 SHARD_WAIT_PREV = 1
+SHARD_NO_SIGNAL = 2
 SHARD_PAD_WORDS = 16
 IPC_HANDLE_BYTES = 64
 HOST_IO = X_HOST | Y_HOST

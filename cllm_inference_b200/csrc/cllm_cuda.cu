@@ -93,6 +93,10 @@ struct DeviceInfo {
     // Q4_K rows of 16..32 super-blocks on the lane-per-super-block loop
     // (environment CLLM_GEMV_SB=0: the lane-per-unit loop instead).
     int gemv_sb = 1;
+    // Row-sharded calls announce their round from a separate one-warp kernel
+    // after the GEMV (1) or from the GEMV's last CTA (0; environment
+    // CLLM_SHARD_SIGNAL_KERNEL).
+    int shard_signal_kernel = 1;
 };
 
 std::mutex g_mu;
@@ -138,6 +142,7 @@ int ensure_device(int* out_dev) {
         if (const char* v = std::getenv("CLLM_GEMV_CTAS_PER_SM")) di.gemv_ctas_per_sm = std::atoi(v) == 1 ? 1 : 2;
         if (const char* v = std::getenv("CLLM_HOSTIO_DIRECT")) di.hostio_direct = std::atoi(v) & 3;
         if (const char* v = std::getenv("CLLM_GEMV_SB")) di.gemv_sb = std::atoi(v) != 0;
+        if (const char* v = std::getenv("CLLM_SHARD_SIGNAL_KERNEL")) di.shard_signal_kernel = std::atoi(v) != 0;
         di.ready = true;
     }
     *out_dev = dev;
@@ -1323,7 +1328,9 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     if (n_rows <= 0) return CLLM_OK;
     if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !y_peers)
         return fail(CLLM_ERR_INVALID_ARG, "%s: bad group (world %d, rank %d)", fname, world, rank);
-    if (flags & ~CLLM_SHARD_WAIT_PREV) return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
+    if (flags & ~(CLLM_SHARD_WAIT_PREV | CLLM_SHARD_NO_SIGNAL))
+        return fail(CLLM_ERR_INVALID_ARG, "%s: unknown flags 0x%x", fname, flags);
+    const bool announce = signal_pads && !(flags & CLLM_SHARD_NO_SIGNAL);
     if (signal_pads && !epoch) return fail(CLLM_ERR_INVALID_ARG, "%s: signal pads without an epoch word", fname);
     if ((flags & CLLM_SHARD_WAIT_PREV) && !signal_pads)
         return fail(CLLM_ERR_INVALID_ARG, "%s: CLLM_SHARD_WAIT_PREV needs the signal pads", fname);
@@ -1340,7 +1347,7 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
             return fail(CLLM_ERR_INVALID_ARG, "%s: null signal pad of rank %d", fname, q);
     }
     if (rows == 0) {  // nothing to compute; still announce the round
-        if (!signal_pads) return CLLM_OK;
+        if (!announce) return CLLM_OK;
         ShardSignal sg{};
         for (int q = 0; q < world; ++q) sg.pads[q] = signal_pads[q];
         sg.epoch = epoch;
@@ -1404,6 +1411,7 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
         p.sepoch = epoch;
         p.srank = rank;
         p.swait = (wait_prev && pl.fused && !use_image) ? 1 : 0;
+        p.sarrive = (announce && !di.shard_signal_kernel) ? 1 : 0;
     }
     if (use_image) {
         const bool w = wait_prev && signal_pads;
@@ -1418,7 +1426,19 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
                                      const_cast<int32_t*>(p.bs), const_cast<uint8_t*>(p.fl), di, st))
             return rc;
     }
-    return launch_gemv(type, false, n_rows, pl, p, st);
+    if (int rc = launch_gemv(type, false, n_rows, pl, p, st)) return rc;
+    if (announce && di.shard_signal_kernel) {
+        // A programmatic dependent of the GEMV: the kernel boundary orders the
+        // GEMV's peer stores before its system-scope fence and release stores,
+        // so the GEMV's CTAs end without per-CTA fences and counting.
+        ShardSignal sg{};
+        for (int q = 0; q < world; ++q) sg.pads[q] = signal_pads[q];
+        sg.epoch = epoch;
+        sg.world = world;
+        sg.rank = rank;
+        if (int rc = launch_shard_kernel(shard_signal_kernel, st, sg)) return rc;
+    }
+    return CLLM_OK;
 }
 
 int cllm_cuda_shard_wait(const uint32_t* own_pad, const uint32_t* epoch, int world, void* stream) {

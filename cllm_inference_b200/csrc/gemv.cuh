@@ -67,6 +67,7 @@ struct GemvParams {
     uint32_t* spads[kMaxPeers];
     uint32_t* sepoch;     // this rank's epoch word (last completed round)
     int srank;
+    int sarrive;          // the grid's last CTA announces the round (else a separate kernel or nobody)
     int swait;            // wait for every rank to have completed *sepoch before reading x
     // FUSED with image != nullptr: the activations were quantized by
     // act_image_kernel into `image` (row masks, then the shared-memory layout);
@@ -1322,7 +1323,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(const GemvPara
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * stg);
     }
-    if (p.spads[0]) {
+    if (p.spads[0] && p.sarrive) {
         named_barrier_sync(kGemvThreads);
         shard_arrive_cta(p);
     }

@@ -182,13 +182,18 @@ class RowShardGroup:
         out.copy_(y)
         return out
 
-    def matmul_unread(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None, chain: bool = False):
+    def matmul_unread(self, x, sw: ShardedWeight, n_rows: int = 1, bias=None, chain: bool = False,
+                      wait: bool = True, signal: bool = True):
         """matmul without the copy-out: returns a view of the group's y buffer,
         valid until the call after next overwrites it.  Each call first waits
         (on the GPU) for every rank to have finished the previous call, so x
-        may be the previous call's output.  chain=True skips the wait for this
-        call's own completion: its y may then only be read by the next call of
-        this group (or after sync())."""
+        may be the previous call's output; wait=False skips that wait for a
+        call whose x does not depend on the previous call (k and v after q,
+        up after gate).  chain=True skips the wait for this call's own
+        completion: its y may then only be read by the next call of this group
+        (or after sync()).  signal=False: the call does not announce its
+        round (a following signalling call announces both); only for a call
+        whose output the next call does not wait on, and never with chain=False."""
         import torch
 
         if n_rows > self.max_rows or sw.out_dim > self.max_out:
@@ -201,8 +206,11 @@ class RowShardGroup:
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(sw.data.data_ptr()), sw.type,
             ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, sw.in_dim, sw.out_dim,
             self.rank, self.world, n_rows, self._yptrs[buf], None if solo else self._sigptrs,
-            None if solo else ctypes.c_void_p(self._epoch_ptr), 0 if solo else _lib.SHARD_WAIT_PREV, st))
+            None if solo else ctypes.c_void_p(self._epoch_ptr),
+            (_lib.SHARD_WAIT_PREV if (wait and not solo) else 0) | (0 if signal else _lib.SHARD_NO_SIGNAL), st))
         if not chain:
+            if not signal:
+                raise ValueError("signal=False needs chain=True")
             self.sync()
         return self._y[buf][:n_rows * sw.out_dim].view(n_rows, sw.out_dim)
 

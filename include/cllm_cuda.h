@@ -224,9 +224,9 @@ int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* 
  *
  * Completion.  signal_pads (NULL: none) are every rank's signal pads
  * (CLLM_SHARD_PAD_WORDS zero-initialised uint32 each, peer-mapped) and epoch
- * this rank's zero-initialised epoch word: the call's last warp then
- * announces "this rank's slice of round epoch+1 has landed" to every rank
- * and advances *epoch.  y is complete on a rank once every rank has
+ * this rank's zero-initialised epoch word: once the GEMV has finished, the
+ * call announces "this rank's slice of round epoch+1 has landed" to every
+ * rank (a one-warp kernel after the GEMV) and advances *epoch.  y is complete on a rank once every rank has
  * announced the round: cllm_cuda_shard_wait waits for that, and a following
  * row-sharded call given CLLM_SHARD_WAIT_PREV waits for it before it reads
  * its x (so chained projections need no separate wait).  Without signal
@@ -234,6 +234,12 @@ int cllm_cuda_shard_rows(int out_dim, int world, int rank, int* row_begin, int* 
  * of signalling calls.  A rank whose slice is empty still signals. */
 #define CLLM_SHARD_PAD_WORDS 16
 #define CLLM_SHARD_WAIT_PREV 1u
+/* The call does not announce its round (signal pads still needed for
+ * CLLM_SHARD_WAIT_PREV).  For a call whose output the next call does not wait
+ * on (q and k before v, gate before up, which read the same x): the round is
+ * announced by the next signalling call, whose completion implies this one's.
+ * Every rank must skip the same calls. */
+#define CLLM_SHARD_NO_SIGNAL 2u
 int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int type, const float* bias,
                                     int in_dim, int out_dim, int rank, int world, int n_rows,
                                     float* const* y_peers, uint32_t* const* signal_pads, uint32_t* epoch,
