@@ -159,6 +159,41 @@ def test_rowshard_signals_every_rank(lib, world, k):
             assert torch.equal(ys[r], ref)
 
 
+def test_rowshard_no_signal_calls_leave_the_round(lib):
+    """CLLM_SHARD_NO_SIGNAL: a call that nobody waits on (k after q, up after
+    gate) neither advances the epoch nor touches the pads; the following
+    signalling call announces the round for both, and a later
+    CLLM_SHARD_WAIT_PREV sees both complete.  Emulated ranks run one after
+    another: every wait depends only on earlier launches."""
+    t, k, n, m, world = synth.Q4_K, 4096, 300, 1, 2
+    ws = [synth.make_weights(t, n, k, seed=11 + i) for i in range(2)]
+    x = to_dev(synth.make_activations(m, k, 5))
+    refs = [_full(lib, x, to_dev(w), t, k, n, m) for w in ws]
+    parts = [[to_dev(np.ascontiguousarray(sharded.shard_weight_bytes(w, t, k, n, world, r))) for r in range(world)]
+             for w in ws]
+    pads = _pads(world)
+    epochs = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(world)]
+    for rnd in range(1, 3):
+        ys = [[torch.full((m, n), float("nan"), device="cuda") for _ in range(world)] for _ in range(2)]
+        for r in range(world):
+            first = (_lib.SHARD_WAIT_PREV if rnd > 1 else 0) | _lib.SHARD_NO_SIGNAL
+            _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(parts[0][r]), t, None, k, n, r, world, m,
+                                                           _ptrs(ys[0]), _ptrs(pads), dptr(epochs[r]), first,
+                                                           stream()))
+            torch.cuda.synchronize()
+            assert int(epochs[r].item()) == rnd - 1  # the no-signal call left the round alone
+            _lib.check(lib.cllm_cuda_matmul_quant_rowshard(dptr(x), dptr(parts[1][r]), t, None, k, n, r, world, m,
+                                                           _ptrs(ys[1]), _ptrs(pads), dptr(epochs[r]), 0, stream()))
+        for r in range(world):
+            _lib.check(lib.cllm_cuda_shard_wait(dptr(pads[r]), dptr(epochs[r]), world, stream()))
+        torch.cuda.synchronize()
+        _lib.check(lib.cllm_cuda_check_device_status())
+        for r in range(world):
+            assert int(epochs[r].item()) == rnd
+            assert pads[r][:world].tolist() == [rnd] * world
+            assert torch.equal(ys[0][r], refs[0]) and torch.equal(ys[1][r], refs[1])
+
+
 def test_rowshard_empty_slice_still_signals(lib):
     """More ranks than rows: rank 2 of 3 owns no row of a 2-row matrix, yet its
     call announces the round, so the others' waits do not run out."""
