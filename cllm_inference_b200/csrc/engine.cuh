@@ -239,6 +239,7 @@ struct Engine {
     int pcap = 0;
     float *X = nullptr, *H = nullptr, *Q = nullptr, *K = nullptr, *V = nullptr, *A = nullptr, *TMP = nullptr;
     float *G = nullptr, *U = nullptr;
+    float *QKV = nullptr, *GU = nullptr;  // row-interleaved outputs of the grouped q|k|v and gate|up GEMMs
     cudaGraphExec_t step_exec = nullptr;
     std::vector<int> cached;
     int seq_len = 0;
@@ -252,7 +253,7 @@ struct Engine {
         if (step_exec) cudaGraphExecDestroy(step_exec);
         if (st) cudaStreamSynchronize(st);
         for (void* p : allocs) cudaFree(p);
-        for (float* p : {X, H, Q, K, V, A, TMP, G, U}) if (p) cudaFree(p);
+        for (float* p : {X, H, Q, K, V, A, TMP, G, U, QKV, GU}) if (p) cudaFree(p);
         if (part_ml) cudaFree(part_ml);
         if (part_acc) cudaFree(part_acc);
         if (tokens_dev) cudaFree(tokens_dev);
@@ -493,7 +494,8 @@ inline int enqueue_step(Engine& e) {
         float* kc = e.kc + (size_t)l * kv_layer;
         float* vc = e.vc + (size_t)l * kv_layer;
         if (int rc_ = pdl(rope_kv_kernel, dim3(dim3(1, c.n_head + c.n_head_kv)), dim3(c.head_dim / 2), e.st,
-            e.q, e.k, e.v, c.n_head, c.n_head_kv, c.head_dim, e.rope, pos, 0, kc, vc)) return rc_;
+            (const float*)e.q, e.q_dim(), e.q, (const float*)e.k, (const float*)e.v, e.kv_dim(), c.n_head,
+            c.n_head_kv, c.head_dim, e.rope, pos, 0, kc, vc)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = attention(e, e.q, kc, vc, pos, 0, 1, e.n_chunks(), e.att)) return rc;
         if (int rc = mm(e, e.att, L.wo, e.x, 1, e.x)) return rc;  // x += W_o att (residual as the bias)
@@ -525,7 +527,7 @@ inline int set_state(Engine& e, int pos, int token, int count) {
 inline int grow_prefill(Engine& e, int T) {
     if (T <= e.pcap) return CLLM_OK;
     const Config& c = e.cfg;
-    for (float** p : {&e.X, &e.H, &e.Q, &e.K, &e.V, &e.A, &e.TMP, &e.G, &e.U}) {
+    for (float** p : {&e.X, &e.H, &e.Q, &e.K, &e.V, &e.A, &e.TMP, &e.G, &e.U, &e.QKV, &e.GU}) {
         if (*p) cudaFree(*p);
         *p = nullptr;
     }
@@ -540,6 +542,8 @@ inline int grow_prefill(Engine& e, int T) {
     CLLM_CUDA_TRY(cudaMalloc(&e.V, te * e.kv_dim() * 4));
     CLLM_CUDA_TRY(cudaMalloc(&e.G, te * c.n_ff * 4));
     CLLM_CUDA_TRY(cudaMalloc(&e.U, te * c.n_ff * 4));
+    CLLM_CUDA_TRY(cudaMalloc(&e.QKV, te * (e.q_dim() + 2 * e.kv_dim()) * 4));
+    CLLM_CUDA_TRY(cudaMalloc(&e.GU, te * 2 * c.n_ff * 4));
     if ((int)te > e.tokens_cap) {
         if (e.tokens_dev) cudaFree(e.tokens_dev);
         e.tokens_dev = nullptr;
@@ -570,21 +574,39 @@ inline int run_prefill(Engine& e, const int* tokens, int T, int pos0) {
         const Layer& L = e.layers[l];
         if (int rc_ = pdl(rmsnorm_kernel, dim3(T), dim3(kNormThreads), e.st, e.X, L.attn_norm, c.n_embd, c.norm_eps, e.H)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
-        if (int rc = mm(e, e.H, L.wq, L.bq, T, e.Q)) return rc;
-        if (int rc = mm(e, e.H, L.wk, L.bk, T, e.K)) return rc;
-        if (int rc = mm(e, e.H, L.wv, L.bv, T, e.V)) return rc;
+        // q|k|v as one GEMM where the three matrices are contiguous (rows of q_dim +
+        // 2 kv_dim per token, one activation preparation, a wider grid)
+        const float *qs = e.Q, *ks = e.K, *vs = e.V;
+        int ldq = e.q_dim(), ldkv = e.kv_dim();
+        if (L.wqkv.rows) {
+            if (int rc = mm(e, e.H, L.wqkv, nullptr, T, e.QKV)) return rc;
+            qs = e.QKV;
+            ks = e.QKV + e.q_dim();
+            vs = ks + e.kv_dim();
+            ldq = ldkv = e.q_dim() + 2 * e.kv_dim();
+        } else {
+            if (int rc = mm(e, e.H, L.wq, L.bq, T, e.Q)) return rc;
+            if (int rc = mm(e, e.H, L.wk, L.bk, T, e.K)) return rc;
+            if (int rc = mm(e, e.H, L.wv, L.bv, T, e.V)) return rc;
+        }
         float* kc = e.kc + (size_t)l * kv_layer;
         float* vc = e.vc + (size_t)l * kv_layer;
         if (int rc_ = pdl(rope_kv_kernel, dim3(dim3(T, c.n_head + c.n_head_kv)), dim3(c.head_dim / 2), e.st,
-            e.Q, e.K, e.V, c.n_head, c.n_head_kv, c.head_dim, e.rope, nullptr, pos0, kc, vc)) return rc_;
+            qs, ldq, e.Q, ks, vs, ldkv, c.n_head, c.n_head_kv, c.head_dim, e.rope, nullptr, pos0, kc, vc)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
         if (int rc = attention(e, e.Q, kc, vc, nullptr, pos0, T, chunks, e.A)) return rc;
         if (int rc = mm(e, e.A, L.wo, nullptr, T, e.TMP)) return rc;
         if (int rc_ = pdl(add_kernel, dim3(grid_for(ne)), dim3(256), e.st, e.X, e.TMP, ne)) return rc_;
         if (int rc_ = pdl(rmsnorm_kernel, dim3(T), dim3(kNormThreads), e.st, e.X, L.ffn_norm, c.n_embd, c.norm_eps, e.H)) return rc_;
-        if (int rc = mm(e, e.H, L.wg, nullptr, T, e.G)) return rc;
-        if (int rc = mm(e, e.H, L.wu, nullptr, T, e.U)) return rc;
-        if (int rc_ = pdl(silu_mul_kernel, dim3(grid_for((int64_t)T * c.n_ff)), dim3(256), e.st, e.G, e.U, (int64_t)T * c.n_ff)) return rc_;
+        if (L.wgu.rows) {  // gate|up as one GEMM, rows of 2 n_ff per token
+            if (int rc = mm(e, e.H, L.wgu, nullptr, T, e.GU)) return rc;
+            if (int rc_ = pdl(silu_mul_rows_kernel, dim3((unsigned)std::min(8, (c.n_ff + 1023) / 1024), (unsigned)T),
+                              dim3(256), e.st, e.G, (const float*)e.GU, c.n_ff)) return rc_;
+        } else {
+            if (int rc = mm(e, e.H, L.wg, nullptr, T, e.G)) return rc;
+            if (int rc = mm(e, e.H, L.wu, nullptr, T, e.U)) return rc;
+            if (int rc_ = pdl(silu_mul_kernel, dim3(grid_for((int64_t)T * c.n_ff)), dim3(256), e.st, e.G, e.U, (int64_t)T * c.n_ff)) return rc_;
+        }
         if (int rc = mm(e, e.G, L.wd, nullptr, T, e.TMP)) return rc;
         if (int rc_ = pdl(add_kernel, dim3(grid_for(ne)), dim3(256), e.st, e.X, e.TMP, ne)) return rc_;
         CLLM_CUDA_TRY(cudaGetLastError());
@@ -958,7 +980,8 @@ int cllm_cuda_rope_kv(float* q, const float* k, const float* v, int n_tok, int n
         return cllm::fail(CLLM_ERR_INVALID_ARG, "rope_kv: bad arguments");
     if (n_tok == 0) return CLLM_OK;
     cllm::eng::rope_kv_kernel<<<dim3(n_tok, n_head + n_head_kv), head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
-        q, k, v, n_head, n_head_kv, head_dim, reinterpret_cast<const float2*>(table), nullptr, pos0, k_cache, v_cache);
+        q, n_head * head_dim, q, k, v, n_head_kv * head_dim, n_head, n_head_kv, head_dim,
+        reinterpret_cast<const float2*>(table), nullptr, pos0, k_cache, v_cache);
     CLLM_CUDA_TRY(cudaGetLastError());
     return CLLM_OK;
 }

@@ -81,28 +81,32 @@ __global__ void embed_kernel(const uint8_t* __restrict__ table, int type, int64_
 // positions base + t (base = *pos_dev + pos0), and the append of the rotated
 // k and of v to this layer's cache rows.  rope[p][i] = (cos, sin) of
 // p / theta^(i/half).  grid (T, n_head + n_kv), block hd/2.
-__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-                               int n_head, int n_kv, int hd, const float2* __restrict__ rope,
-                               const int* __restrict__ pos_dev, int pos0, float* __restrict__ kc,
-                               float* __restrict__ vc) {
+// q, k, v: token rows of ldq / ldkv floats (the separate projections, or
+// the row-interleaved output of one grouped q|k|v GEMM); the rotated q goes
+// to qo as dense [T][n_head * hd] rows (qo == q with ldq == q_dim: in place).
+__global__ void rope_kv_kernel(const float* q, int ldq, float* qo, const float* __restrict__ k,
+                               const float* __restrict__ v, int ldkv, int n_head, int n_kv, int hd,
+                               const float2* __restrict__ rope, const int* __restrict__ pos_dev, int pos0,
+                               float* __restrict__ kc, float* __restrict__ vc) {
     pdl_start();
     const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x, half = hd >> 1;
     const int pos = (pos_dev ? *pos_dev : 0) + pos0 + t;
     const float2 cs = rope[(int64_t)pos * half + i];
     const int q_dim = n_head * hd, kv_dim = n_kv * hd;
     if (h < n_head) {
-        float* qh = q + (int64_t)t * q_dim + h * hd;
+        const float* qh = q + (int64_t)t * ldq + h * hd;
+        float* qd = qo + (int64_t)t * q_dim + h * hd;
         const float x0 = qh[i], x1 = qh[i + half];
-        qh[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        qh[i + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+        qd[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+        qd[i + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
     } else {
         const int kh = h - n_head;
-        const float* kr = k + (int64_t)t * kv_dim + kh * hd;
+        const float* kr = k + (int64_t)t * ldkv + kh * hd;
         float* kd = kc + (int64_t)pos * kv_dim + kh * hd;
         const float x0 = kr[i], x1 = kr[i + half];
         kd[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
         kd[i + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        const float* vr = v + (int64_t)t * kv_dim + kh * hd;
+        const float* vr = v + (int64_t)t * ldkv + kh * hd;
         float* vd = vc + (int64_t)pos * kv_dim + kh * hd;
         vd[i] = vr[i];
         vd[i + half] = vr[i + half];
@@ -389,6 +393,18 @@ __global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float v = g[i];
         g[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[i]);
+    }
+}
+
+// out[t][i] = silu(gu[t][i]) * gu[t][n + i] for the row-interleaved output of
+// one grouped gate|up GEMM (rows of 2n); the operations of silu_mul_kernel.
+__global__ void silu_mul_rows_kernel(float* __restrict__ out, const float* __restrict__ gu, int n) {
+    pdl_start();
+    const int64_t t = blockIdx.y;
+    const float* g = gu + t * 2 * n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float v = g[i];
+        out[t * n + i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), g[n + i]);
     }
 }
 
