@@ -494,6 +494,18 @@ bool prefill_eligible(int type, const void* w, int64_t row_bytes, int K, int n_r
            (row_bytes & 15) == 0;
 }
 
+// prefill_prep_kernel: 64 blocks per CTA and step; float4 loads when x allows.
+int launch_prefill_prep(const float* x, int K, int64_t blocks, __half* a16, float* dxx, float* dxT, int64_t mp,
+                        uint8_t* flags, const DeviceInfo& di, cudaStream_t st) {
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((blocks + 63) / 64, 16LL * di.sms));
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0)
+        prefill_prep_kernel<true><<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, dxT, mp, flags);
+    else
+        prefill_prep_kernel<false><<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, dxT, mp, flags);
+    CLLM_CUDA_TRY(cudaGetLastError());
+    return CLLM_OK;
+}
+
 // Tokens per row of the block-major dx arrays of the prefill (16-byte rows for their tensor maps).
 inline int64_t q6_dx_pitch(int M) { return ((int64_t)M + 3) & ~int64_t(3); }
 
@@ -529,8 +541,7 @@ int launch_prefill_q6k(const float* x, const uint8_t* w, int64_t row_bytes, cons
     const int splits = q6_splits(M, N, K, di.sms);
     float* ypart = splits > 1 ? reinterpret_cast<float*>(flags + align256((size_t)(M * nb))) : nullptr;
     const int64_t blocks = (int64_t)M * nb;
-    const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
-    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, nullptr, dxT, mp, flags);
+    if (int rc = launch_prefill_prep(x, K, blocks, a16, nullptr, dxT, mp, flags, di, st)) return rc;
     CLLM_CUDA_TRY(cudaGetLastError());
     CUtensorMap map_x, map_w, map_dx;
     if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxT, (uint64_t)M, (uint64_t)nb, kTcBM, 8,
@@ -565,8 +576,7 @@ int launch_prefill(int type, const float* x, const uint8_t* w, int64_t row_bytes
     float* dxx = reinterpret_cast<float*>(ws + off_dx);  // [nb][mp][2]: (dx, dx*bsum), block-major
     const int64_t mp = q6_dx_pitch(M);
     const int64_t blocks = (int64_t)M * (K / 32);
-    const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 16LL * di.sms);
-    prefill_prep_kernel<<<(unsigned)grid, 256, 0, st>>>(x, K, blocks, a16, dxx, nullptr, mp, nullptr);
+    if (int rc = launch_prefill_prep(x, K, blocks, a16, dxx, nullptr, mp, nullptr, di, st)) return rc;
     CLLM_CUDA_TRY(cudaGetLastError());
     CUtensorMap map_a, map_w, map_dx;
     if (int rc = make_map_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dxx, (uint64_t)(2 * M), (uint64_t)nb,

@@ -571,38 +571,76 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // (bit-exact, as quantize_q8_0_kernel), writing q_x as fp16 and, where the
 // pointers are given, the pairs (dx, dx*bsum) block-major [nb][mp][2] (Q4_K),
 // dx block-major [nb][mp] (Q6_K) and a flag per block that holds a -128 (Q6_K).
+template <bool VEC>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ x, int64_t n,
                                                            int64_t total_blocks, __half* __restrict__ a16,
                                                            float* __restrict__ dxx, float* __restrict__ dxT,
                                                            int64_t mp, uint8_t* __restrict__ flags) {
-    const int lane = threadIdx.x & 31;
+    // four lanes per 32-value block, eight values each (two float4 loads when
+    // VEC: x 16-byte aligned); a warp takes eight blocks per step
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int64_t nb = n >> 5;
-    for (int64_t blk = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; blk < total_blocks; blk += nwarps) {
-        const int64_t r = blk / nb, b = blk - r * nb;
-        const int64_t e = r * n + b * 32 + lane;
-        const float v = x[e];
-        const float a = fabsf(v);
-        float amax = (a > 0.0f) ? a : 0.0f;
+    for (int64_t base = 8 * warp0; base < total_blocks; base += 8 * nwarps) {
+        const int64_t blk = base + (lane >> 2);
+        const bool valid = blk < total_blocks;
+        const int64_t r = valid ? blk / nb : 0, b = valid ? blk - r * nb : 0;
+        const int64_t e0 = r * n + b * 32 + 8 * sub;
+        float v[8];
+        if (valid) {
+            if constexpr (VEC) {
+                const float4 p0 = __ldg(reinterpret_cast<const float4*>(x + e0));
+                const float4 p1 = __ldg(reinterpret_cast<const float4*>(x + e0) + 1);
+                v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+                v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+            } else {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+                for (int k = 0; k < 8; ++k) v[k] = __ldg(x + e0 + k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = 0.0f;
+        }
+        // max of |x| over the block's non-NaN values (fmaxf keeps the number)
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
         const float d = amax / 127.0f;
         const float id = (d != 0.0f) ? 1.0f / d : 0.0f;
-        const float vv = v * id;
-        int q = fabsf(vv) < 4194304.0f ? __float_as_int(vv + 12582912.0f) - 0x4B400000 : INT32_MIN;
-        q = q > 127 ? 127 : (q < -128 ? -128 : q);
-        a16[e] = __int2half_rn(q);
-        int s = q;
+        int q[8], s8 = 0;
+        bool has_min = false;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if (lane == 0 && dxx) {  // (dx, dx*bsum) pairs, [nb][mp][2]
-            dxx[2 * (b * mp + r)] = d;
-            dxx[2 * (b * mp + r) + 1] = d * (float)s;
+        for (int k = 0; k < 8; ++k) {
+            const float vv = v[k] * id;
+            int qi = fabsf(vv) < 4194304.0f ? __float_as_int(vv + 12582912.0f) - 0x4B400000 : INT32_MIN;
+            qi = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
+            q[k] = qi;
+            s8 += qi;
+            has_min |= qi == -128;
         }
-        if (lane == 0 && dxT) dxT[b * mp + r] = d;
-        if (flags) {
-            const unsigned neg = __ballot_sync(0xFFFFFFFFu, q == -128);
-            if (lane == 0) flags[r * nb + b] = neg ? 1 : 0;
+        int s = s8 + __shfl_xor_sync(0xFFFFFFFFu, s8, 1);
+        s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+        const unsigned neg = (__ballot_sync(0xFFFFFFFFu, has_min) >> (lane & ~3)) & 0xFu;
+        if (!valid) continue;
+        __half2 h[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) h[k] = __halves2half2(__int2half_rn(q[2 * k]), __int2half_rn(q[2 * k + 1]));
+        if constexpr (VEC) {
+            *reinterpret_cast<uint4*>(a16 + e0) = *reinterpret_cast<const uint4*>(h);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) *reinterpret_cast<__half2*>(a16 + e0 + 2 * k) = h[k];
+        }
+        if (sub == 0) {
+            if (dxx) {  // (dx, dx*bsum) pairs, [nb][mp][2]
+                dxx[2 * (b * mp + r)] = d;
+                dxx[2 * (b * mp + r) + 1] = d * (float)s;
+            }
+            if (dxT) dxT[b * mp + r] = d;
+            if (flags) flags[r * nb + b] = neg ? 1 : 0;
         }
     }
 }

@@ -140,3 +140,22 @@ def test_prefill_q6k_config3_down_shape(cuda, lib, oracle, m):
     rows = _tile_samples(n, 128, np.random.default_rng(9))
     yo, ab = oracle.matmul(x, G.row_subset(w, synth.row_bytes(t, k), rows), t, k, len(rows), with_abs=True)
     G.assert_rows_close(y[:, rows], yo, ab, REL_TOL, f"config 3 down as Q6_K, M={m}")
+
+
+@pytest.mark.parametrize("t,k", [(synth.Q4_K, 1024), (synth.Q6_K, 2048)])
+def test_prefill_unaligned_activations(cuda, lib, oracle, t, k):
+    """x 4 bytes past a 16-byte boundary: the activation preparation falls
+    back to scalar loads; the tensor-core GEMM itself is unaffected."""
+    n, m = 136, 70
+    w = synth.make_weights(t, n, k, seed=k + 3, q6_scale_max=128)
+    x = synth.make_activations(m, k, seed=k + 4)
+    wt, wp = G.dev_bytes(w)
+    assert plan(lib, wp, t, k, n, m)[1] == 2
+    xb = torch.zeros(m * k + 4, dtype=torch.float32, device="cuda")
+    xb[1:1 + m * k] = torch.from_numpy(x.reshape(-1)).cuda()
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xb.data_ptr() + 4), wp, t, None, k, n, m, G.dptr(y), 0,
+                                          G.stream()))
+    torch.cuda.synchronize()
+    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+    G.assert_rows_close(y.cpu().numpy(), yo, ab, REL_TOL, f"unaligned x {synth.NAMES[t]}")
