@@ -207,6 +207,48 @@ def test_host_io_pinned_in_place(cuda, lib, oracle, t, k, n, m, xoff, yoff):
         assert np.isnan(yh[:yoff].numpy()).all() and np.isnan(yh[yoff + m * n:].numpy()).all()
 
 
+def test_host_io_graph_rebuilt_after_memory_moves(cuda, lib, oracle):
+    """A cached host-I/O call graph points at the workspace and, with
+    CLLM_W_HOST, at the registered weight copy.  When the workspace grows (a
+    large prefill call in between) or the registration is replaced, the next
+    call with the same arguments must rebuild its graph and stay correct."""
+    import ctypes
+
+    t, k, n = synth.Q4_K, 4096, 256
+    w = synth.make_weights(t, n, k, seed=41)
+    x = synth.make_activations(1, k, 42)
+    xh = torch.from_numpy(x.reshape(-1).copy()).pin_memory()
+    yh = torch.empty(n, dtype=torch.float32).pin_memory()
+    yo, ab = oracle.matmul(x, w, t, k, n, with_abs=True)
+    base = w.ctypes.data
+
+    def call():
+        yh.fill_(float("nan"))
+        _lib.check(lib.cllm_cuda_matmul_quant(ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(base), t, None, k, n, 1,
+                                              ctypes.c_void_p(yh.data_ptr()), _lib.HOST_IO | _lib.W_HOST, None))
+        G.assert_rows_close(yh.numpy().reshape(1, n), yo, ab, REL_TOL, "host io graph")
+
+    _lib.check(lib.cllm_cuda_register_weights(ctypes.c_void_p(base), w.nbytes, None))
+    try:
+        call()
+        call()  # replayed
+        # grow the workspace: a 2048-token tcgen05 prefill over in_dim 14336
+        wb = synth.make_weights_torch(synth.Q6_K, 128, 14336, seed=43)
+        xb = torch.from_numpy(synth.make_activations(2048, 14336, 44)).cuda()
+        yb = torch.empty(2048 * 128, device="cuda")
+        _lib.check(lib.cllm_cuda_matmul_quant(G.dptr(xb), G.dptr(wb), synth.Q6_K, None, 14336, 128, 2048, G.dptr(yb),
+                                              0, G.stream()))
+        torch.cuda.synchronize()
+        call()
+        # replace the registration of the same host range
+        _lib.check(lib.cllm_cuda_unregister_weights(ctypes.c_void_p(base)))
+        _lib.check(lib.cllm_cuda_register_weights(ctypes.c_void_p(base), w.nbytes, None))
+        call()
+        call()
+    finally:
+        _lib.check(lib.cllm_cuda_unregister_weights(ctypes.c_void_p(base)))
+
+
 def test_empty_and_degenerate(cuda, lib, oracle):
     t = synth.Q4_K
     w = synth.make_weights(t, 8, 256, 1)
