@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
 //   * the last CTA of each KV head to finish (a counter per KV head, reset by
 //     that CTA) merges the chunks as attn_combine_kernel.
 constexpr int kDecChunk = 32;
+constexpr int kDecMergeChunks = 256;  // chunks the merge keeps in shared memory (contexts up to 8192)
 template <int HD, int REP>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* __restrict__ q,
                                                                    const float* __restrict__ k,
@@ -347,18 +348,51 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const float* 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int i = threadIdx.x; i < REP * HD; i += kAttnThreads) {
-        const int h = kvh * REP + i / HD, d = i % HD;
-        const int64_t base = (int64_t)h * n_chunks;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nc; ++cc) M = fmaxf(M, __ldcg(part_ml + 2 * (base + cc)));
-        float L = 0.0f, acc = 0.0f;
-        for (int cc = 0; cc < nc; ++cc) {
-            const float wgt = expf(__fsub_rn(__ldcg(part_ml + 2 * (base + cc)), M));
-            L = fmaf(wgt, __ldcg(part_ml + 2 * (base + cc) + 1), L);
-            acc = fmaf(wgt, __ldcg(part_acc + (base + cc) * HD + d), acc);
+    if (nc <= kDecMergeChunks) {
+        // the chunk weights w_c = exp(m_c - M) and L = sum_c w_c l_c once per
+        // head (warp r: head r), then every output element's sum over chunks
+        // with its loads issued ahead of the FMAs
+        __shared__ float s_w[REP][kDecMergeChunks];
+        __shared__ float s_L[REP];
+        for (int r = warp; r < REP; r += kAttnThreads / 32) {
+            const int64_t base = (int64_t)(kvh * REP + r) * n_chunks;
+            float M = -INFINITY;
+            for (int cc = lane; cc < nc; cc += 32) M = fmaxf(M, __ldcg(part_ml + 2 * (base + cc)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+            float L = 0.0f;
+            for (int cc = lane; cc < nc; cc += 32) {
+                const float wgt = expf(__fsub_rn(__ldcg(part_ml + 2 * (base + cc)), M));
+                s_w[r][cc] = wgt;
+                L = fmaf(wgt, __ldcg(part_ml + 2 * (base + cc) + 1), L);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+            if (lane == 0) s_L[r] = L;
         }
-        out[(int64_t)h * HD + d] = __fdiv_rn(acc, L);
+        __syncthreads();
+        for (int i = threadIdx.x; i < REP * HD; i += kAttnThreads) {
+            const int r = i / HD, d = i % HD;
+            const float* pa = part_acc + (int64_t)(kvh * REP + r) * n_chunks * HD + d;
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int cc = 0; cc < nc; ++cc) acc = fmaf(s_w[r][cc], __ldcg(pa + (int64_t)cc * HD), acc);
+            out[(int64_t)(kvh * REP + r) * HD + d] = __fdiv_rn(acc, s_L[r]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < REP * HD; i += kAttnThreads) {
+            const int h = kvh * REP + i / HD, d = i % HD;
+            const int64_t base = (int64_t)h * n_chunks;
+            float M = -INFINITY;
+            for (int cc = 0; cc < nc; ++cc) M = fmaxf(M, __ldcg(part_ml + 2 * (base + cc)));
+            float L = 0.0f, acc = 0.0f;
+            for (int cc = 0; cc < nc; ++cc) {
+                const float wgt = expf(__fsub_rn(__ldcg(part_ml + 2 * (base + cc)), M));
+                L = fmaf(wgt, __ldcg(part_ml + 2 * (base + cc) + 1), L);
+                acc = fmaf(wgt, __ldcg(part_acc + (base + cc) * HD + d), acc);
+            }
+            out[(int64_t)h * HD + d] = __fdiv_rn(acc, L);
+        }
     }
     if (threadIdx.x == 0) counters[kvh] = 0;
 }
