@@ -7,7 +7,7 @@
 // in a CUDA graph that reads the input token and the position from device
 // memory and ends with the greedy argmax, so generation replays the graph
 // with no host round trip per token.  Prefill batches T tokens through
-// matmul_quant_batch (the tcgen05 GEMM for Q4_K weights, T >= 64).
+// matmul_quant_batch (the tcgen05 GEMMs for Q4_K and Q6_K weights, T >= 32).
 //
 // Included at the end of cllm_cuda.cu (one translation unit), after the C ABI
 // it calls.

@@ -166,7 +166,7 @@ int cllm_cuda_dequantize_f16(const void* src, int type, int64_t n, uint16_t* dst
 /* Launch plan cllm_cuda_matmul_quant would use for these arguments (device
  * weights at w): info[0] kernels launched per call, [1] the dot kernel: 0
  * direct loads, 1 bulk-copy (TMA) ring GEMV, 2 tcgen05 tensor-core GEMM
- * (Q4_K batches of >= 64 rows), 3 the dequantize-and-float-dot fallback
+ * (Q4_K and Q6_K batches of >= 32 rows), 3 the dequantize-and-float-dot fallback
  * (types without an integer dot kernel), [2] 1 if activation quantization is fused
  * into the dot kernel, [3] weight rows per tile, [4] warps per row, [5]
  * pipeline stages, [6] CTAs, [7] dynamic shared memory bytes.  No

@@ -1,4 +1,4 @@
-"""Batched prefill (matmul_quant_batch, n_rows >= 64) on the tcgen05 GEMM
+"""Batched prefill (matmul_quant_batch, n_rows >= 32) on the tcgen05 GEMM
 against the oracle, with the same row tolerance as the decode path:
 |y_gpu - y_ref| <= 1e-5 * sum over the row's per-block float terms of |term|."""
 import ctypes
@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 REL_TOL = 1e-5
 
 # (K, N, M): a single tile, ragged token and row tiles, several super-blocks
-SHAPES = [(256, 128, 64), (256, 200, 100), (1024, 300, 129), (4096, 256, 128), (4096, 300, 257)]
+SHAPES = [(256, 128, 32), (1024, 136, 48), (256, 128, 64), (256, 200, 100), (1024, 300, 129), (4096, 256, 128),
+          (4096, 300, 257)]
 
 
 def plan(lib, w_ptr, t, k, n, m):
@@ -34,6 +35,14 @@ def test_prefill_q4k_tcgen05(cuda, lib, oracle, k, n, m):
     y = G.matmul(lib, x, w, t, k, n, bias=bias)
     yo, ab = oracle.matmul(x, w, t, k, n, bias=bias, with_abs=True)
     G.assert_rows_close(y, yo, ab, REL_TOL, f"prefill {k}x{n} m={m}")
+
+
+def test_prefill_threshold(cuda, lib):
+    """31 rows run the GEMV in chunks, 32 rows the tensor-core GEMM."""
+    for t, k in ((synth.Q4_K, 4096), (synth.Q6_K, 4096)):
+        w = torch.empty(synth.row_bytes(t, k) * 64, dtype=torch.uint8, device="cuda")
+        assert plan(lib, G.dptr(w), t, k, 64, 31)[1] != 2
+        assert plan(lib, G.dptr(w), t, k, 64, 32)[1] == 2
 
 
 def test_prefill_matches_decode_rows(cuda, lib):
@@ -83,7 +92,8 @@ def test_prefill_config3_exact_shape(cuda, lib, oracle, m):
 # Q6_K: K a multiple of 2048 keeps its 210-byte-per-super-block rows 16-byte
 # multiples (the tensor map's row pitch); the full int8 scale range makes
 # sc * (q6 - 32) exceed fp16's exact integers, which the kernel must not need.
-Q6_SHAPES = [(2048, 128, 64), (2048, 200, 100), (4096, 300, 129), (4096, 256, 257), (6144, 136, 192)]
+Q6_SHAPES = [(2048, 128, 32), (4096, 200, 47), (2048, 128, 64), (2048, 200, 100), (4096, 300, 129),
+             (4096, 256, 257), (6144, 136, 192)]
 
 
 @pytest.mark.parametrize("k,n,m", Q6_SHAPES)
