@@ -32,7 +32,7 @@ namespace cllm {
 
 // From 32 activation rows the tensor-core GEMM beats the GEMV in chunks of 8
 // rows (measured on the 8B shapes: at 32 rows the GEMV's four chunks take
-// 1.2-4x the GEMM's time, except q/o and k/v where the two tie).
+// 1.2-3x the GEMM's time, except on the 1024-row k/v matrices, where the two tie).
 constexpr int kTcMinRows = 32;
 constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 64;
 constexpr int kTcStA = 4, kTcStB = 4, kTcStRaw = 2, kTcDBuf = 3;
